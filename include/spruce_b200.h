@@ -1,0 +1,180 @@
+/*
+ * spruce_b200.h -- C ABI of the B200 (sm_100a) SPRUCE sparse-prefill path.
+ *
+ * Plain pointers, element strides and sizes; no torch or CUDA types.  All
+ * pointers are device pointers unless noted, `stream` is a cudaStream_t (NULL
+ * = legacy default stream).  No entry point allocates device memory or
+ * synchronises the stream: work is enqueued and the call returns.  Inputs are
+ * borrowed; outputs are written in place.
+ *
+ * Return value: SPRUCE_OK or an SPRUCE_ERR_* code; spruce_last_error() gives
+ * the calling thread's message for the last failure.  The Python layer maps
+ * SPRUCE_ERR_INVALID / SPRUCE_ERR_UNSUPPORTED to ValueError and the rest to
+ * RuntimeError, as the reference raises ValueError for contract violations
+ * (kernels/seerattention_direct_index_triton.py:350-372).
+ *
+ * Shapes follow the reference's tensors: q [B, Hq, T, D], k/v [B, Hkv, T, D]
+ * (any strides with a unit last stride, e.g. views of token-major
+ * [B, T, H, D] projections), selected_blocks int32 [B, L, G, qb, K] with
+ * qb = ceil(T / 64) and G = Hkv (interfaces/selected_blocks_spec.md).
+ */
+#ifndef SPRUCE_B200_H
+#define SPRUCE_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SPRUCE_OK 0
+#define SPRUCE_ERR_INVALID 1     /* argument violates the contract         */
+#define SPRUCE_ERR_UNSUPPORTED 2 /* outside the kernels' coverage           */
+#define SPRUCE_ERR_CUDA 3        /* CUDA runtime / driver error             */
+#define SPRUCE_ERR_WORKSPACE 4   /* workspace smaller than required         */
+
+/* Bits kernels OR into the optional device status word (uint32). */
+#define SPRUCE_STATUS_TIMEOUT 1u   /* a bounded pipeline wait ran out       */
+#define SPRUCE_STATUS_EMPTY_ROW 2u /* a selected_blocks row had no block    */
+
+#define SPRUCE_DTYPE_F32 0
+#define SPRUCE_DTYPE_BF16 1
+#define SPRUCE_DTYPE_F16 2
+
+#define SPRUCE_BLOCK 64 /* tokens per block; the reference's kernels require 64 */
+
+#if defined(__GNUC__)
+#define SPRUCE_API __attribute__((visibility("default")))
+#else
+#define SPRUCE_API
+#endif
+
+/* Message for the calling thread's last failed call ("" if none). */
+SPRUCE_API const char *spruce_last_error(void);
+
+/* ABI version of this library (bumped on any signature change). */
+SPRUCE_API int spruce_abi_version(void);
+
+/*
+ * _group_avg_tokens, teacher/chunked_extract.py:75-80: average the H/G query
+ * heads of each group per token.  x [B, H, T, D] with element strides
+ * x_strides[4]; out [B, G, T, D] contiguous, same dtype.  Bit-exact with the
+ * reference: fp32 sum over heads in order, fp32 divide, one rounding.
+ */
+SPRUCE_API int spruce_group_avg_tokens(const void *x, const int64_t x_strides[4], int dtype, int64_t B, int64_t H,
+                            int64_t T, int64_t D, int64_t G, void *out, void *stream);
+
+/*
+ * _proto_pool_seq, teacher/chunked_extract.py:27-72, mean prototype (P = 1):
+ * x [B, H, T, D] (strided) -> out [B, H, nb, 1, D] contiguous, nb =
+ * ceil(T / block), block = 64.  Bit-exact with the reference's rounding points
+ * (16-row fp32 partial sums, sum rounded to dtype, divided by the real row
+ * count of the block).  P > 1 returns SPRUCE_ERR_UNSUPPORTED.
+ */
+SPRUCE_API int spruce_proto_pool(const void *x, const int64_t x_strides[4], int dtype, int64_t B, int64_t H, int64_t T,
+                      int64_t D, int64_t block, int64_t P, void *out, void *stream);
+
+/*
+ * Selector inputs of one layer in one launch: pooled_q = block mean of the
+ * group-averaged queries, pooled_k = block mean of the keys, both
+ * [B, Hkv, qb, D] contiguous in the input dtype.  Equivalent to
+ * _proto_pool_seq(_group_avg_tokens(q, Hkv), 64, 1) and
+ * _proto_pool_seq(k, 64, 1) (teacher/chunked_extract.py:170-171).
+ */
+SPRUCE_API int spruce_pool_qk(const void *q, const int64_t q_strides[4], const void *k, const int64_t k_strides[4],
+                   int dtype, int64_t B, int64_t Hq, int64_t Hkv, int64_t T, int64_t D, void *pooled_q,
+                   void *pooled_k, void *stream);
+
+/*
+ * FlatGate projection, selector/gate.py:120-127 (project_queries /
+ * project_keys) and :47-48: out[n, :] = fp32(x[n, :]) @ W, x [N, D] contiguous
+ * in dtype, W [D, P] fp32 contiguous, out [N, P] fp32.  Fixed fma order over D.
+ */
+SPRUCE_API int spruce_gate_project(const void *x, int dtype, int64_t N, int64_t D, const float *W, int64_t P, float *out,
+                        void *stream);
+
+/*
+ * FlatGate.forward with one prototype, selector/gate.py:80-101:
+ * out[r, i, j] = (qp[r, i, :] . kp[r, j, :]) / sqrt(P) for R score matrices
+ * (layers x groups), qp [R, qb, P], kp [R, kb, P], out [R, qb, kb], fp32.
+ */
+SPRUCE_API int spruce_gate_scores(const float *qp, const float *kp, int64_t R, int64_t qb, int64_t kb, int64_t P,
+                       float *out, void *stream);
+
+/*
+ * Fused flat-gate selection: scores (as spruce_gate_scores), causal /
+ * sink / local-window masking, top-W with W = K - (local_window + 1) -
+ * sink_blocks (ties to the lowest block id) and packing to selected_blocks
+ * rows, without materialising the score matrix.  Equivalent to
+ * topk + selected_ids_to_blocks(ids, K, local_window, key_blocks=qb,
+ * sink_blocks) (scripts/route_overrides.py:187-205,
+ * scripts/export_selected_blocks.py:80-175).  qp/kp [B, G, qb, P] fp32
+ * contiguous; row (b, g, q) is written at out + b*out_strides[0] +
+ * g*out_strides[1] + q*out_strides[2] (K contiguous int32).
+ */
+SPRUCE_API int spruce_gate_select(const float *qp, const float *kp, int64_t B, int64_t G, int64_t qb, int64_t P, int64_t K,
+                       int64_t local_window, int64_t sink_blocks, int32_t *out, const int64_t out_strides[3],
+                       void *stream);
+
+/* Bytes of workspace spruce_select_blocks needs for this shape. */
+SPRUCE_API int64_t spruce_select_workspace_bytes(int64_t B, int64_t Hkv, int64_t T, int64_t D, int64_t P, int dtype);
+
+/*
+ * Whole flat selector for one layer: spruce_pool_qk -> spruce_gate_project
+ * (Wq, Wk [D, P] fp32) -> spruce_gate_select.  Pooled features and
+ * projections live in the caller's `workspace` (see
+ * spruce_select_workspace_bytes).
+ */
+SPRUCE_API int spruce_select_blocks(const void *q, const int64_t q_strides[4], const void *k, const int64_t k_strides[4],
+                         int dtype, int64_t B, int64_t Hq, int64_t Hkv, int64_t T, int64_t D, const float *Wq,
+                         const float *Wk, int64_t P, int64_t K, int64_t local_window, int64_t sink_blocks,
+                         int32_t *out, const int64_t out_strides[3], void *workspace, int64_t workspace_bytes,
+                         void *stream);
+
+/*
+ * selected_ids_to_blocks, scripts/export_selected_blocks.py:80-175:
+ * ids [R, qb, C] int64 (R = layers x groups, contiguous) -> out [R, qb, K]
+ * int32.  Same policy: forced local window and sink blocks, deduplicated
+ * causal nonlocal ids of which the smallest fill the remaining slots,
+ * sorted, -1 padded.
+ */
+SPRUCE_API int spruce_pack_selected_ids(const int64_t *ids, int64_t R, int64_t qb, int64_t C, int64_t K,
+                             int64_t local_window, int64_t key_blocks, int64_t sink_blocks, int32_t *out,
+                             void *stream);
+
+/*
+ * validate_selected_blocks rules, interfaces/validator.py:7-62, on the GPU:
+ * sel [B, L, G, qb, K] int32 contiguous.  Writes to result[0] (device int64)
+ * the smallest violating row (b, l, g, q) flattened, times 8, plus the first
+ * violated rule (1 causal, 2 unsorted, 3 duplicate, 4 missing local block,
+ * 5 non-trailing pad), or -1 if the tensor is valid.  The host formats the
+ * reference's AssertionError message from that row.
+ */
+SPRUCE_API int spruce_validate_selected_blocks(const int32_t *sel, int64_t B, int64_t L, int64_t G, int64_t qb, int64_t K,
+                                    int64_t local_window, int64_t *result, void *stream);
+
+/*
+ * Causal GQA block-sparse attention over selected key blocks,
+ * kernels/seerattention_direct_index_triton.py:339-416 (and the math of
+ * sparse/attention.py:143-274).  q [B, Hq, T, D], k/v [B, Hkv, T, D] with
+ * element strides *_strides[4] (unit last stride); indices [B, Hkv, qb, Kw]
+ * int32 with strides idx_strides[4] (unit last stride), -1 = padding;
+ * out is written through the LOGICAL [B, Hq, T, D] strides out_strides[4]
+ * (pass the strides of a [B, T, Hq, D] tensor viewed as [B, Hq, T, D] to get
+ * the reference's token-major output).  scale multiplies q.k (D**-0.5 in the
+ * reference).  bf16/fp16 run the tcgen05 kernel (D in {64, 128}); fp32 runs
+ * a CUDA-core fp32 kernel.  Block ids < 0 are skipped and ids above the query
+ * block contribute nothing (causal mask); a row left empty yields zeros and
+ * raises SPRUCE_STATUS_EMPTY_ROW in *status when status is not NULL.
+ */
+SPRUCE_API int spruce_sparse_attention_fwd(const void *q, const int64_t q_strides[4], const void *k,
+                                const int64_t k_strides[4], const void *v, const int64_t v_strides[4],
+                                const int32_t *indices, const int64_t idx_strides[4], void *out,
+                                const int64_t out_strides[4], int dtype, int64_t B, int64_t Hq, int64_t Hkv,
+                                int64_t T, int64_t D, int64_t Kw, float scale, uint32_t *status, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPRUCE_B200_H */

@@ -1,0 +1,405 @@
+/*
+ * CPU restatement of the SPRUCE sparse-prefill hot path -- TEST INFRASTRUCTURE.
+ *
+ * This file is the parity checker for the CUDA product path, never part of
+ * it: only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline /
+ * --impl reference legs load the library built from it.
+ *
+ * Parity is pinned: tests/golden/make_golden.py runs the reference's own torch
+ * functions on seeded inputs and commits their outputs under tests/golden/;
+ * tests/test_oracle_golden.py checks this restatement against them (indices
+ * bit-exact, pooled features bit-exact, attention within fp32 round-off).
+ *
+ * Element types: 0 = float32, 1 = bfloat16, 2 = float16 (16-bit values are
+ * passed as raw uint16 storage).  Rounding to 16-bit types is round-to-
+ * nearest-even, as torch does.
+ *
+ * Compile with -ffp-contract=off: every rounding point below is deliberate.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+enum { DT_F32 = 0, DT_BF16 = 1, DT_F16 = 2 };
+
+static inline float bf16_bits_to_f32(uint16_t h) {
+    uint32_t u = (uint32_t)h << 16;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+static inline uint16_t f32_to_bf16_bits(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40u);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
+static inline float f16_bits_to_f32(uint16_t h) {
+    _Float16 x;
+    memcpy(&x, &h, 2);
+    return (float)x;
+}
+
+static inline uint16_t f32_to_f16_bits(float f) {
+    _Float16 x = (_Float16)f;
+    uint16_t h;
+    memcpy(&h, &x, 2);
+    return h;
+}
+
+static inline float load_elem(const void *p, int dtype, size_t i) {
+    if (dtype == DT_F32) return ((const float *)p)[i];
+    if (dtype == DT_BF16) return bf16_bits_to_f32(((const uint16_t *)p)[i]);
+    return f16_bits_to_f32(((const uint16_t *)p)[i]);
+}
+
+static inline void store_elem(void *p, int dtype, size_t i, float v) {
+    if (dtype == DT_F32) ((float *)p)[i] = v;
+    else if (dtype == DT_BF16) ((uint16_t *)p)[i] = f32_to_bf16_bits(v);
+    else ((uint16_t *)p)[i] = f32_to_f16_bits(v);
+}
+
+/* Value of v after a round trip through dtype. */
+static inline float round_to(int dtype, float v) {
+    if (dtype == DT_F32) return v;
+    if (dtype == DT_BF16) return bf16_bits_to_f32(f32_to_bf16_bits(v));
+    return f16_bits_to_f32(f32_to_f16_bits(v));
+}
+
+/*
+ * Group average of query heads, teacher/chunked_extract.py:75-80
+ * (_group_avg_tokens: x.view(b, G, H//G, L, d).mean(dim=2)).
+ * torch's CPU mean over the head axis sums the H/G heads in order in fp32,
+ * divides by H/G in fp32 and rounds once to the input dtype.
+ * x: [B, H, T, D] contiguous; out: [B, G, T, D].
+ */
+void oracle_group_avg(const void *x, int dtype, int64_t B, int64_t H, int64_t T,
+                      int64_t D, int64_t G, void *out) {
+    const int64_t rep = H / G;
+    const float frep = (float)rep;
+    for (int64_t b = 0; b < B; ++b)
+        for (int64_t g = 0; g < G; ++g)
+            for (int64_t t = 0; t < T; ++t)
+                for (int64_t d = 0; d < D; ++d) {
+                    float acc = 0.0f;
+                    for (int64_t h = 0; h < rep; ++h) {
+                        size_t src = (((size_t)b * H + g * rep + h) * T + t) * D + d;
+                        acc = acc + load_elem(x, dtype, src);
+                    }
+                    size_t dst = (((size_t)b * G + g) * T + t) * D + d;
+                    store_elem(out, dtype, dst, acc / frep);
+                }
+}
+
+/*
+ * Block mean (prototype 0 of _proto_pool_seq), teacher/chunked_extract.py:33-46.
+ * The reference zero-pads the ragged tail, multiplies by the validity mask,
+ * sums the 64 rows of each block and divides by the real row count:
+ *   mean = (xb * vf).sum(dim=3) / counts
+ * torch's CPU sum over that (non-innermost) axis accumulates 16 consecutive
+ * rows at a time in fp32, then adds the chunk totals in order; the sum is
+ * rounded to the input dtype, then divided by the count in fp32 and rounded
+ * again.  Verified bit-exact against the reference for fp32, bf16 and fp16.
+ * x: [B, H, T, D] contiguous; out: [B, H, nb, D] with nb = ceil(T / block).
+ */
+void oracle_block_mean(const void *x, int dtype, int64_t B, int64_t H, int64_t T,
+                       int64_t D, int64_t block, void *out) {
+    const int64_t nb = (T + block - 1) / block;
+    for (int64_t b = 0; b < B; ++b)
+        for (int64_t h = 0; h < H; ++h)
+            for (int64_t i = 0; i < nb; ++i) {
+                const int64_t t0 = i * block;
+                const int64_t count = (T - t0) < block ? (T - t0) : block;
+                for (int64_t d = 0; d < D; ++d) {
+                    float total = 0.0f;
+                    for (int64_t c = 0; c < block; c += 16) {
+                        float chunk = 0.0f;
+                        for (int64_t r = c; r < c + 16 && r < block; ++r) {
+                            float v = 0.0f;
+                            if (r < count)
+                                v = load_elem(x, dtype, (((size_t)b * H + h) * T + t0 + r) * D + d);
+                            chunk = chunk + v;
+                        }
+                        total = total + chunk;
+                    }
+                    float s = round_to(dtype, total);
+                    size_t dst = (((size_t)b * H + h) * nb + i) * D + d;
+                    store_elem(out, dtype, dst, s / (float)count);
+                }
+            }
+}
+
+/*
+ * Gate projection, selector/gate.py:47-48 (einsum "gqid,dp->gqip").
+ * Accumulation order is fixed: acc = fma(x[d], W[d][p], acc) for d = 0..D-1,
+ * the order the CUDA kernel uses, so the two agree bit for bit.
+ * x: [N, D] in dtype (converted to fp32 as selector/targets.py:34 does);
+ * W: [D, P] fp32; out: [N, P] fp32.
+ */
+void oracle_project(const void *x, int dtype, int64_t N, int64_t D, const float *W,
+                    int64_t P, float *out) {
+#pragma omp parallel for schedule(static)
+    for (int64_t n = 0; n < N; ++n)
+        for (int64_t p = 0; p < P; ++p) {
+            float acc = 0.0f;
+            for (int64_t d = 0; d < D; ++d)
+                acc = fmaf(load_elem(x, dtype, (size_t)n * D + d), W[(size_t)d * P + p], acc);
+            out[(size_t)n * P + p] = acc;
+        }
+}
+
+/*
+ * FlatGate score with one prototype, selector/gate.py:57 and :101:
+ *   s[i][j] = (qp_i . kp_j) / sqrt(p)
+ * dot product as fma over p = 0..P-1; the division is a true fp32 division by
+ * (float)sqrt(P) (torch divides by the python float math.sqrt(P)).
+ * qp: [nq, P], kp: [nk, P]; out: [nq, nk].
+ */
+void oracle_scores(const float *qp, int64_t nq, const float *kp, int64_t nk, int64_t P,
+                   float *out) {
+    const float denom = (float)sqrt((double)P);
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < nq; ++i)
+        for (int64_t j = 0; j < nk; ++j) {
+            float acc = 0.0f;
+            for (int64_t p = 0; p < P; ++p)
+                acc = fmaf(qp[(size_t)i * P + p], kp[(size_t)j * P + p], acc);
+            out[(size_t)i * nk + j] = acc / denom;
+        }
+}
+
+/* Order-preserving map from fp32 to uint32: a > b  <=>  key(a) > key(b).
+ * NaN maps above +inf, as torch.topk treats NaN as the largest value. */
+static inline uint32_t order_key(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return 0xffffffffu;
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+typedef struct { uint32_t key; int32_t idx; } cand_t;
+
+static int cand_cmp(const void *a, const void *b) {
+    const cand_t *x = (const cand_t *)a, *y = (const cand_t *)b;
+    if (x->key != y->key) return x->key > y->key ? -1 : 1;   /* larger score first */
+    return x->idx < y->idx ? -1 : (x->idx > y->idx);          /* then lowest block id */
+}
+
+/*
+ * Flat-gate top-k selection packed into selected_blocks rows.
+ *
+ * Restates the composition the reference uses for flat top-k routes
+ * (scripts/route_overrides.py:187-205 teacher_topk_routes, with the flat
+ * FlatGate scores of benchmarks/compare_dense_sparse_live_tree.py:314-320):
+ *   mask future, sink and local-window blocks; ids = topk(W) with
+ *   W = K - (local_window + 1) - sink_blocks;
+ *   selected_ids_to_blocks(ids, K, local_window, key_blocks=kb, sink_blocks)
+ *   (scripts/export_selected_blocks.py:80-175).
+ * Per row q this is: sink blocks j < min(sink, kb) with j < q - local_window,
+ * local blocks max(0, q - local_window)..q, and the W best-scoring candidates
+ * j in [sink, q - local_window) -- ties broken toward the lowest block id,
+ * which torch.topk leaves unspecified -- emitted in increasing order and
+ * padded with -1 to K.
+ * scores: [R, qb, kb] fp32 (R independent score matrices, e.g. KV groups);
+ * out: [R, qb, K] int32.  Returns 0, or 1 if K cannot hold the forced blocks.
+ */
+int oracle_select_rows(const float *scores, int64_t R, int64_t qb, int64_t kb, int64_t K,
+                       int64_t local_window, int64_t sink_blocks, int32_t *out) {
+    if (K < local_window + 1 + sink_blocks) return 1;
+    const int64_t sink = sink_blocks < kb ? sink_blocks : kb;
+    int64_t W = K - (local_window + 1) - sink_blocks;
+    if (W > kb) W = kb;
+    int rc = 0;
+#pragma omp parallel
+    {
+        cand_t *cand = (cand_t *)malloc(sizeof(cand_t) * (size_t)(kb > 0 ? kb : 1));
+        unsigned char *keep = (unsigned char *)malloc((size_t)(kb > 0 ? kb : 1));
+        if (!cand || !keep) {
+#pragma omp atomic write
+            rc = 2;
+        }
+#pragma omp for schedule(dynamic, 16)
+        for (int64_t row = 0; row < R * qb; ++row) {
+            if (!cand || !keep) continue;
+            const int64_t q = row % qb;
+            const float *s = scores + (size_t)row * kb;
+            int32_t *o = out + (size_t)row * K;
+            memset(keep, 0, (size_t)kb);
+            int64_t n = 0;
+            for (int64_t j = sink; j < q - local_window && j < kb; ++j) {
+                cand[n].key = order_key(s[j]);
+                cand[n].idx = (int32_t)j;
+                ++n;
+            }
+            if (n > W) qsort(cand, (size_t)n, sizeof(cand_t), cand_cmp);
+            const int64_t take = n < W ? n : W;
+            for (int64_t c = 0; c < take; ++c) keep[cand[c].idx] = 1;
+            for (int64_t j = 0; j < sink && j < q - local_window; ++j) keep[j] = 1;
+            for (int64_t j = q - local_window < 0 ? 0 : q - local_window; j <= q && j < kb; ++j)
+                keep[j] = 1;
+            int64_t w = 0;
+            for (int64_t j = 0; j < kb && j <= q && w < K; ++j)
+                if (keep[j]) o[w++] = (int32_t)j;
+            for (; w < K; ++w) o[w] = -1;
+        }
+        free(cand);
+        free(keep);
+    }
+    return rc;
+}
+
+/*
+ * selected_ids_to_blocks restatement, scripts/export_selected_blocks.py:80-175.
+ * ids: [R, qb, C] int64 candidate ids (any value; invalid ones are ignored);
+ * out: [R, qb, K] int32.  Policy per row q:
+ *   nonlocal candidates: 0 <= id < kb, id <= q, id < q - local_window,
+ *   id >= sink (export_selected_blocks.py:125-129), deduplicated, and only the
+ *   `remaining` SMALLEST kept (:138-146) where
+ *   remaining = K - min(q + 1, local_window + 1) - clamp(q - local_window, 0, sink);
+ *   plus sink ids j < sink with j < q - local_window (:164-170) and local ids
+ *   q - local_window .. q that are >= 0 (:153-158); sorted, first K, -1 pad.
+ * Returns 0, or 1 on the argument errors the reference raises ValueError for.
+ */
+int oracle_pack_ids(const int64_t *ids, int64_t R, int64_t qb, int64_t C, int64_t K,
+                    int64_t local_window, int64_t kb, int64_t sink_blocks, int32_t *out) {
+    if (K < 1 || local_window < 0 || sink_blocks < 0 || kb < 1) return 1;
+    if (K < local_window + 1 + sink_blocks) return 1;
+    const int64_t sink = sink_blocks < kb ? sink_blocks : kb;
+    const int64_t span = qb > kb ? qb : kb;
+    int rc = 0;
+#pragma omp parallel
+    {
+        unsigned char *mark = (unsigned char *)malloc((size_t)span + 1);
+        if (!mark) {
+#pragma omp atomic write
+            rc = 2;
+        }
+#pragma omp for schedule(static)
+        for (int64_t row = 0; row < R * qb; ++row) {
+            if (!mark) continue;
+            const int64_t q = row % qb;
+            const int64_t *r = ids + (size_t)row * C;
+            int32_t *o = out + (size_t)row * K;
+            memset(mark, 0, (size_t)span + 1);
+            for (int64_t c = 0; c < C; ++c) {
+                const int64_t id = r[c];
+                if (id >= 0 && id < kb && id <= q && id < q - local_window && id >= sink)
+                    mark[id] = 1;
+            }
+            int64_t local_count = q + 1 < local_window + 1 ? q + 1 : local_window + 1;
+            int64_t sink_count = q - local_window;
+            if (sink_count < 0) sink_count = 0;
+            if (sink_count > sink) sink_count = sink;
+            int64_t remaining = K - local_count - sink_count;
+            int64_t kept = 0;
+            for (int64_t j = 0; j < span; ++j)
+                if (mark[j]) {
+                    if (kept < remaining) ++kept;
+                    else mark[j] = 0;
+                }
+            for (int64_t j = 0; j < sink; ++j)
+                if (j < q - local_window) mark[j] = 1;
+            for (int64_t j = q - local_window; j <= q; ++j)
+                if (j >= 0) mark[j] = 1;
+            int64_t w = 0;
+            for (int64_t j = 0; j < span && w < K; ++j)
+                if (mark[j]) o[w++] = (int32_t)j;
+            for (; w < K; ++w) o[w] = -1;
+        }
+        free(mark);
+    }
+    return rc;
+}
+
+/*
+ * Block-sparse causal GQA attention, sparse/attention.py:143-274
+ * (sparse_prefill_attention_forward without the HF mask and residual
+ * summaries): for each batch, KV group g and query block, the key tokens of
+ * the row's non-negative block ids (in row order, tokens >= T dropped,
+ * :204-207), fp32 scores q.k / sqrt(D) (:217-219), future tokens masked
+ * (:222-224), softmax in fp32 (:266), fp32 P.V (:267-269).  A row whose
+ * tokens are all masked gets zeros (the reference would raise on an empty
+ * row, :194-199; the direct-index kernels return zeros/NaN).
+ * q: [B, Hq, T, D] fp32, k/v: [B, Hkv, T, D] fp32, idx: [B, Hkv, qb, Kw]
+ * int32; out: [B, T, Hq, D] fp32 (token-major like the reference's return).
+ */
+void oracle_sparse_attention(const float *q, const float *k, const float *v,
+                             const int32_t *idx, int64_t B, int64_t Hq, int64_t Hkv,
+                             int64_t T, int64_t D, int64_t Kw, int64_t block, float scale,
+                             float *out) {
+    const int64_t qb = (T + block - 1) / block;
+    const int64_t rep = Hq / Hkv;
+#pragma omp parallel
+    {
+        int64_t *keys = (int64_t *)malloc(sizeof(int64_t) * (size_t)(Kw * block + 1));
+        float *s = (float *)malloc(sizeof(float) * (size_t)(Kw * block + 1));
+        double *acc = (double *)malloc(sizeof(double) * (size_t)D);
+#pragma omp for schedule(dynamic, 1)
+        for (int64_t unit = 0; unit < B * Hkv * qb; ++unit) {
+            const int64_t b = unit / (Hkv * qb);
+            const int64_t g = (unit / qb) % Hkv;
+            const int64_t i = unit % qb;
+            const int32_t *row = idx + (((size_t)b * Hkv + g) * qb + i) * Kw;
+            int64_t nk = 0;
+            for (int64_t c = 0; c < Kw; ++c) {
+                if (row[c] < 0) continue;
+                for (int64_t t = 0; t < block; ++t) {
+                    int64_t key = (int64_t)row[c] * block + t;
+                    if (key < T) keys[nk++] = key;
+                }
+            }
+            const float *kg = k + ((size_t)b * Hkv + g) * T * D;
+            const float *vg = v + ((size_t)b * Hkv + g) * T * D;
+            for (int64_t hh = 0; hh < rep; ++hh) {
+                const int64_t h = g * rep + hh;
+                for (int64_t t = i * block; t < (i + 1) * block && t < T; ++t) {
+                    const float *qr = q + (((size_t)b * Hq + h) * T + t) * D;
+                    float m = -INFINITY;
+                    for (int64_t c = 0; c < nk; ++c) {
+                        if (keys[c] > t) { s[c] = -INFINITY; continue; }
+                        const float *kr = kg + (size_t)keys[c] * D;
+                        float dot = 0.0f;
+                        for (int64_t d = 0; d < D; ++d) dot += qr[d] * kr[d];
+                        s[c] = dot * scale;
+                        if (s[c] > m) m = s[c];
+                    }
+                    float *o = out + (((size_t)b * T + t) * Hq + h) * D;
+                    if (m == -INFINITY) {
+                        for (int64_t d = 0; d < D; ++d) o[d] = 0.0f;
+                        continue;
+                    }
+                    double l = 0.0;
+                    for (int64_t d = 0; d < D; ++d) acc[d] = 0.0;
+                    for (int64_t c = 0; c < nk; ++c) {
+                        if (s[c] == -INFINITY) continue;
+                        const double p = exp((double)s[c] - (double)m);
+                        l += p;
+                        const float *vr = vg + (size_t)keys[c] * D;
+                        for (int64_t d = 0; d < D; ++d) acc[d] += p * (double)vr[d];
+                    }
+                    for (int64_t d = 0; d < D; ++d) o[d] = (float)(acc[d] / l);
+                }
+            }
+        }
+        free(keys);
+        free(s);
+        free(acc);
+    }
+}
+
+/* Number of threads the OpenMP runtime will use (for the CPU-baseline report). */
+int oracle_num_threads(void) {
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}

@@ -1,0 +1,246 @@
+"""Python front end of the CPU oracle -- TEST INFRASTRUCTURE ONLY.
+
+Wraps ``oracle/_build/liboracle.so`` (built from ``oracle/oracle.c`` by
+``oracle/Makefile``) with numpy/torch-CPU helpers that restate the
+reference's sparse-prefill path end to end:
+
+  _group_avg_tokens      teacher/chunked_extract.py:75-80
+  _proto_pool_seq (P=1)  teacher/chunked_extract.py:27-46
+  FlatGate (P=1)         selector/gate.py:47-57, :101
+  flat top-k + packing   scripts/route_overrides.py:187-205 +
+                         scripts/export_selected_blocks.py:80-175
+  selected_ids_to_blocks scripts/export_selected_blocks.py:80-175
+  validate_selected_blocks interfaces/validator.py:7-62
+  sparse attention       sparse/attention.py:143-274
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs import
+this module; the product path never does.  Parity is pinned by the golden
+vectors under tests/golden/ (made by running the reference itself).
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+import subprocess
+
+import numpy as np
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "_build", "liboracle.so")
+_lib = None
+
+DT_CODE = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
+PAD_VALUE = -1
+
+
+def build() -> str:
+    """Compile the oracle library with its Makefile (idempotent)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        L = ctypes.CDLL(_LIB_PATH)
+        P, I64, F = ctypes.c_void_p, ctypes.c_int64, ctypes.c_float
+        L.oracle_group_avg.argtypes = [P, ctypes.c_int, I64, I64, I64, I64, I64, P]
+        L.oracle_block_mean.argtypes = [P, ctypes.c_int, I64, I64, I64, I64, I64, P]
+        L.oracle_project.argtypes = [P, ctypes.c_int, I64, I64, P, I64, P]
+        L.oracle_scores.argtypes = [P, I64, P, I64, I64, P]
+        L.oracle_select_rows.argtypes = [P, I64, I64, I64, I64, I64, I64, P]
+        L.oracle_select_rows.restype = ctypes.c_int
+        L.oracle_pack_ids.argtypes = [P, I64, I64, I64, I64, I64, I64, I64, P]
+        L.oracle_pack_ids.restype = ctypes.c_int
+        L.oracle_sparse_attention.argtypes = [P, P, P, P, I64, I64, I64, I64, I64, I64, I64, F, P]
+        L.oracle_num_threads.restype = ctypes.c_int
+        _lib = L
+    return _lib
+
+
+def _raw(t: torch.Tensor) -> torch.Tensor:
+    """Contiguous CPU tensor whose storage the C code reads as raw bits."""
+    t = t.detach().cpu().contiguous()
+    if t.dtype in (torch.bfloat16, torch.float16):
+        return t.view(torch.int16)
+    return t
+
+
+def _ptr(t: torch.Tensor) -> int:
+    return t.data_ptr()
+
+
+def num_threads() -> int:
+    return int(lib().oracle_num_threads())
+
+
+def group_avg_tokens(x: torch.Tensor, G: int) -> torch.Tensor:
+    """[b, H, L, d] -> [b, G, L, d] in x's dtype."""
+    b, H, T, d = x.shape
+    src = _raw(x)
+    out = torch.empty((b, G, T, d), dtype=x.dtype)
+    lib().oracle_group_avg(_ptr(src), DT_CODE[x.dtype], b, H, T, d, G, _ptr(_raw_view(out)))
+    return out
+
+
+def _raw_view(t: torch.Tensor) -> torch.Tensor:
+    return t.view(torch.int16) if t.dtype in (torch.bfloat16, torch.float16) else t
+
+
+def block_mean(x: torch.Tensor, block: int = 64) -> torch.Tensor:
+    """[b, H, L, d] -> [b, H, nb, d]: prototype 0 of _proto_pool_seq."""
+    b, H, T, d = x.shape
+    nb = (T + block - 1) // block
+    src = _raw(x)
+    out = torch.empty((b, H, nb, d), dtype=x.dtype)
+    lib().oracle_block_mean(_ptr(src), DT_CODE[x.dtype], b, H, T, d, block, _ptr(_raw_view(out)))
+    return out
+
+
+def proto_pool_seq(x: torch.Tensor, block: int, P: int) -> torch.Tensor:
+    """[b, H, L, d] -> [b, H, nb, P, d] for P = 1 (the mean prototype)."""
+    if P != 1:
+        raise NotImplementedError("the oracle restates the P=1 (mean) prototype only")
+    return block_mean(x, block)[:, :, :, None, :]
+
+
+def project(x: torch.Tensor, W: torch.Tensor) -> torch.Tensor:
+    """x [..., d] (any float dtype) @ W [d, p] fp32 -> fp32 [..., p]."""
+    d, p = W.shape
+    src = _raw(x.reshape(-1, d))
+    Wc = W.detach().float().cpu().contiguous()
+    out = torch.empty((src.shape[0], p), dtype=torch.float32)
+    lib().oracle_project(_ptr(src), DT_CODE[x.dtype], src.shape[0], d, _ptr(Wc), p, _ptr(out))
+    return out.view(*x.shape[:-1], p)
+
+
+def scores(qp: torch.Tensor, kp: torch.Tensor) -> torch.Tensor:
+    """qp [nq, p], kp [nk, p] fp32 -> [nq, nk] = qp.kp / sqrt(p)."""
+    qp = qp.float().contiguous()
+    kp = kp.float().contiguous()
+    out = torch.empty((qp.shape[0], kp.shape[0]), dtype=torch.float32)
+    lib().oracle_scores(_ptr(qp), qp.shape[0], _ptr(kp), kp.shape[0], qp.shape[1], _ptr(out))
+    return out
+
+
+def select_rows(s: torch.Tensor, k_selected: int, local_window: int, sink_blocks: int) -> torch.Tensor:
+    """s [R, qb, kb] fp32 -> int32 [R, qb, K] packed rows (flat top-k policy)."""
+    R, qb, kb = s.shape
+    s = s.float().contiguous()
+    out = torch.empty((R, qb, k_selected), dtype=torch.int32)
+    rc = lib().oracle_select_rows(_ptr(s), R, qb, kb, k_selected, local_window, sink_blocks, _ptr(out))
+    if rc:
+        raise ValueError(
+            f"k_selected={k_selected} cannot fit local window size {local_window + 1} "
+            f"plus {sink_blocks} sink block(s)")
+    return out
+
+
+def selected_ids_to_blocks(selected_ids: torch.Tensor, k_selected: int, local_window: int = 1,
+                           key_blocks: int | None = None, sink_blocks: int = 0) -> torch.Tensor:
+    """[L, G, qb, C] ids -> int32 [1, L, G, qb, K] (reference packing policy)."""
+    L, G, qb, C = selected_ids.shape
+    kb = qb if key_blocks is None else int(key_blocks)
+    ids = selected_ids.detach().cpu().to(torch.int64).contiguous()
+    out = torch.empty((L, G, qb, k_selected), dtype=torch.int32)
+    rc = lib().oracle_pack_ids(_ptr(ids), L * G, qb, C, k_selected, local_window, kb, sink_blocks, _ptr(out))
+    if rc:
+        raise ValueError("invalid packing arguments")
+    return out.unsqueeze(0)
+
+
+def select_blocks(q: torch.Tensor, k: torch.Tensor, wq: torch.Tensor, wk: torch.Tensor,
+                  k_selected: int, local_window: int = 0, sink_blocks: int = 1,
+                  block: int = 64) -> dict:
+    """Full flat selector for one layer.
+
+    q [B, Hq, T, d], k [B, Hkv, T, d] (any strides), wq/wk [d, p] fp32.
+    Returns pooled_q/pooled_k [B, Hkv, qb, d] (input dtype), qp/kp fp32,
+    scores [B, Hkv, qb, qb] fp32 and selected int32 [B, Hkv, qb, K].
+    """
+    B, Hq, T, d = q.shape
+    Hkv = k.shape[1]
+    qg = group_avg_tokens(q, Hkv)
+    pooled_q = block_mean(qg, block)
+    pooled_k = block_mean(k, block)
+    qp = project(pooled_q, wq)
+    kp = project(pooled_k, wk)
+    qb = pooled_q.shape[2]
+    s = torch.stack([scores(qp[b, g], kp[b, g]) for b in range(B) for g in range(Hkv)])
+    sel = select_rows(s, k_selected, local_window, sink_blocks)
+    return {
+        "pooled_q": pooled_q, "pooled_k": pooled_k, "qp": qp, "kp": kp,
+        "scores": s.view(B, Hkv, qb, qb), "selected": sel.view(B, Hkv, qb, k_selected),
+    }
+
+
+def sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices: torch.Tensor,
+                     scale: float | None = None, block: int = 64, out_dtype=None) -> torch.Tensor:
+    """q [B, Hq, T, D], k/v [B, Hkv, T, D], indices int32 [B, Hkv, qb, K].
+
+    Returns [B, T, Hq, D] in ``out_dtype`` (default: q's dtype), computed in
+    fp32 with double-precision softmax sums.
+    """
+    B, Hq, T, D = q.shape
+    Hkv = k.shape[1]
+    if scale is None:
+        scale = D ** -0.5
+    qf = q.detach().float().cpu().contiguous()
+    kf = k.detach().float().cpu().contiguous()
+    vf = v.detach().float().cpu().contiguous()
+    idx = indices.detach().cpu().to(torch.int32).contiguous()
+    out = torch.empty((B, T, Hq, D), dtype=torch.float32)
+    lib().oracle_sparse_attention(_ptr(qf), _ptr(kf), _ptr(vf), _ptr(idx), B, Hq, Hkv, T, D,
+                                  idx.shape[-1], block, float(scale), _ptr(out))
+    return out.to(out_dtype or q.dtype)
+
+
+def validate_selected_blocks(t: torch.Tensor, local_window: int = 1) -> None:
+    """interfaces/validator.py:7-62 restated row by row; raises AssertionError.
+
+    Rows are visited in (b, l, g, q) order and the rules in the reference's
+    order (causal, sorted, duplicates, local window, trailing padding), so the
+    first violation and its message match the reference's.
+    """
+    assert t.dim() == 5, (
+        "Expected 5D tensor [batch, layer, kv_head_group, query_block, "
+        f"K_selected_blocks], got {t.dim()}D with shape {tuple(t.shape)}")
+    assert t.dtype == torch.int32, f"Expected int32, got {t.dtype}"
+    assert local_window >= 0, f"local_window must be >= 0, got {local_window}"
+    a = t.detach().cpu().numpy()
+    B, L, G, Q, K = a.shape
+    for b in range(B):
+        for l in range(L):
+            for g in range(G):
+                for q in range(Q):
+                    row = a[b, l, g, q].tolist()
+                    real = [x for x in row if x != PAD_VALUE]
+                    where = f"[b={b}, l={l}, g={g}, q={q}]"
+                    for block_id in real:
+                        assert block_id <= q, (
+                            f"Causal violation at {where}: block {block_id} is in the future (q={q})")
+                    assert real == sorted(real), f"Not sorted at {where}: {real}"
+                    assert len(real) == len(set(real)), f"Duplicate block IDs at {where}: {real}"
+                    missing = [x for x in range(max(0, q - local_window), q + 1) if x not in real]
+                    assert not missing, (
+                        f"Missing local-window block(s) at {where}: missing {missing}, row={real}")
+                    if PAD_VALUE in row:
+                        first = row.index(PAD_VALUE)
+                        assert all(x == PAD_VALUE for x in row[first:]), (
+                            f"Padding is not trailing-only at {where}: {row}")
+
+
+def dense_causal_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+    """Dense causal GQA attention in fp64 -> [B, T, Hq, D] fp32 (100%-density check)."""
+    B, Hq, T, D = q.shape
+    rep = Hq // k.shape[1]
+    kk = k.double().repeat_interleave(rep, dim=1)
+    vv = v.double().repeat_interleave(rep, dim=1)
+    s = (q.double() @ kk.transpose(-1, -2)) / math.sqrt(D)
+    mask = torch.ones(T, T, dtype=torch.bool).triu(1)
+    s = s.masked_fill(mask, float("-inf"))
+    return (torch.softmax(s, dim=-1) @ vv).transpose(1, 2).float()

@@ -1,0 +1,254 @@
+// extern "C" entry points of libspruce_b200.so (declared in include/spruce_b200.h).
+//
+// Each entry point checks the contract the reference enforces (shape and
+// dtype ValueErrors of kernels/seerattention_direct_index_triton.py:350-372,
+// scripts/export_selected_blocks.py:98-119), plus the alignment the vector
+// loads and TMA need, then enqueues its kernels on `stream`.  Nothing here
+// allocates device memory or synchronises.
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return SPRUCE_OK;
+  return fail(SPRUCE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int elem_size(int dtype) { return dtype == SPRUCE_DTYPE_F32 ? 4 : 2; }
+
+bool valid_dtype(int dtype) {
+  return dtype == SPRUCE_DTYPE_F32 || dtype == SPRUCE_DTYPE_BF16 || dtype == SPRUCE_DTYPE_F16;
+}
+
+// Strides [b, h, t] (element units) must keep every 16-byte row segment aligned.
+bool vec_strides_ok(const int64_t* s, int dtype, int64_t D) {
+  const int64_t vn = 16 / elem_size(dtype);
+  return s[3] == 1 && s[0] % vn == 0 && s[1] % vn == 0 && s[2] % vn == 0 && D % vn == 0;
+}
+
+cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+}  // namespace
+
+extern "C" {
+
+const char* spruce_last_error(void) { return g_last_error.c_str(); }
+
+int spruce_abi_version(void) { return 1; }
+
+int spruce_group_avg_tokens(const void* x, const int64_t x_strides[4], int dtype, int64_t B, int64_t H, int64_t T,
+                            int64_t D, int64_t G, void* out, void* stream) {
+  if (!valid_dtype(dtype)) return fail(SPRUCE_ERR_INVALID, "unsupported dtype code %d", dtype);
+  if (B < 0 || H < 1 || T < 0 || D < 1 || G < 1) return fail(SPRUCE_ERR_INVALID, "bad shape");
+  if (H % G) return fail(SPRUCE_ERR_INVALID, "H=%lld not divisible by G=%lld", (long long)H, (long long)G);
+  if (!aligned16(x) || !aligned16(out) || !vec_strides_ok(x_strides, dtype, D))
+    return fail(SPRUCE_ERR_UNSUPPORTED, "x must be 16-byte aligned with a unit last stride");
+  if (B == 0 || T == 0) return SPRUCE_OK;
+  cudaError_t e;
+  switch (dtype) {
+    case SPRUCE_DTYPE_F32: e = spruce::launch_group_avg<float>(x, x_strides, out, B, H, T, D, G, as_stream(stream)); break;
+    case SPRUCE_DTYPE_BF16:
+      e = spruce::launch_group_avg<__nv_bfloat16>(x, x_strides, out, B, H, T, D, G, as_stream(stream));
+      break;
+    default: e = spruce::launch_group_avg<__half>(x, x_strides, out, B, H, T, D, G, as_stream(stream)); break;
+  }
+  return cuda_status(e, "group_avg launch");
+}
+
+static int pool_jobs(spruce::PoolJob j0, spruce::PoolJob j1, int njobs, int dtype, int64_t B, int64_t T, int64_t D,
+                     void* stream) {
+  cudaError_t e;
+  switch (dtype) {
+    case SPRUCE_DTYPE_F32: e = spruce::launch_pool<float>(j0, j1, njobs, B, T, D, as_stream(stream)); break;
+    case SPRUCE_DTYPE_BF16: e = spruce::launch_pool<__nv_bfloat16>(j0, j1, njobs, B, T, D, as_stream(stream)); break;
+    default: e = spruce::launch_pool<__half>(j0, j1, njobs, B, T, D, as_stream(stream)); break;
+  }
+  return cuda_status(e, "pool launch");
+}
+
+int spruce_proto_pool(const void* x, const int64_t x_strides[4], int dtype, int64_t B, int64_t H, int64_t T,
+                      int64_t D, int64_t block, int64_t P, void* out, void* stream) {
+  if (!valid_dtype(dtype)) return fail(SPRUCE_ERR_INVALID, "unsupported dtype code %d", dtype);
+  if (block != SPRUCE_BLOCK) return fail(SPRUCE_ERR_UNSUPPORTED, "block must be 64, got %lld", (long long)block);
+  if (P != 1) return fail(SPRUCE_ERR_UNSUPPORTED, "only the mean prototype (P=1) is implemented, got P=%lld", (long long)P);
+  if (B < 0 || H < 1 || T < 0 || D < 1 || D > 256) return fail(SPRUCE_ERR_INVALID, "bad shape");
+  if (!aligned16(x) || !aligned16(out) || !vec_strides_ok(x_strides, dtype, D))
+    return fail(SPRUCE_ERR_UNSUPPORTED, "x must be 16-byte aligned with a unit last stride");
+  if (B == 0 || T == 0) return SPRUCE_OK;
+  spruce::PoolJob j{x, x_strides[0], x_strides[1], x_strides[2], out, 1, (int)H};
+  return pool_jobs(j, j, 1, dtype, B, T, D, stream);
+}
+
+int spruce_pool_qk(const void* q, const int64_t q_strides[4], const void* k, const int64_t k_strides[4], int dtype,
+                   int64_t B, int64_t Hq, int64_t Hkv, int64_t T, int64_t D, void* pooled_q, void* pooled_k,
+                   void* stream) {
+  if (!valid_dtype(dtype)) return fail(SPRUCE_ERR_INVALID, "unsupported dtype code %d", dtype);
+  if (B < 0 || Hq < 1 || Hkv < 1 || T < 0 || D < 1 || D > 256) return fail(SPRUCE_ERR_INVALID, "bad shape");
+  if (Hq % Hkv) return fail(SPRUCE_ERR_INVALID, "query heads (%lld) must be divisible by KV heads (%lld)",
+                            (long long)Hq, (long long)Hkv);
+  if (!aligned16(q) || !aligned16(k) || !aligned16(pooled_q) || !aligned16(pooled_k) ||
+      !vec_strides_ok(q_strides, dtype, D) || !vec_strides_ok(k_strides, dtype, D))
+    return fail(SPRUCE_ERR_UNSUPPORTED, "q/k must be 16-byte aligned with a unit last stride");
+  if (B == 0 || T == 0) return SPRUCE_OK;
+  spruce::PoolJob jq{q, q_strides[0], q_strides[1], q_strides[2], pooled_q, (int)(Hq / Hkv), (int)Hkv};
+  spruce::PoolJob jk{k, k_strides[0], k_strides[1], k_strides[2], pooled_k, 1, (int)Hkv};
+  return pool_jobs(jq, jk, 2, dtype, B, T, D, stream);
+}
+
+int spruce_gate_project(const void* x, int dtype, int64_t N, int64_t D, const float* W, int64_t P, float* out,
+                        void* stream) {
+  if (!valid_dtype(dtype)) return fail(SPRUCE_ERR_INVALID, "unsupported dtype code %d", dtype);
+  if (N < 0 || D < 1 || P < 1 || D > 1024) return fail(SPRUCE_ERR_INVALID, "bad projection shape");
+  cudaError_t e;
+  switch (dtype) {
+    case SPRUCE_DTYPE_F32: e = spruce::launch_project<float>(x, N, D, W, P, out, as_stream(stream)); break;
+    case SPRUCE_DTYPE_BF16: e = spruce::launch_project<__nv_bfloat16>(x, N, D, W, P, out, as_stream(stream)); break;
+    default: e = spruce::launch_project<__half>(x, N, D, W, P, out, as_stream(stream)); break;
+  }
+  return cuda_status(e, "projection launch");
+}
+
+int spruce_gate_scores(const float* qp, const float* kp, int64_t R, int64_t qb, int64_t kb, int64_t P, float* out,
+                       void* stream) {
+  if (R < 0 || qb < 0 || kb < 0 || P < 1 || P > 1024) return fail(SPRUCE_ERR_INVALID, "bad score shape");
+  if (R == 0 || qb == 0 || kb == 0) return SPRUCE_OK;
+  return cuda_status(spruce::launch_scores(qp, kp, R, qb, kb, P, out, as_stream(stream)), "score launch");
+}
+
+static int check_select_policy(int64_t K, int64_t lw, int64_t sink) {
+  if (K < 1) return fail(SPRUCE_ERR_INVALID, "k_selected must be >= 1, got %lld", (long long)K);
+  if (lw < 0) return fail(SPRUCE_ERR_INVALID, "local_window must be >= 0, got %lld", (long long)lw);
+  if (sink < 0) return fail(SPRUCE_ERR_INVALID, "sink_blocks must be >= 0, got %lld", (long long)sink);
+  if (K < lw + 1 + sink)
+    return fail(SPRUCE_ERR_INVALID, "k_selected=%lld cannot fit local window size %lld plus %lld sink block(s)",
+                (long long)K, (long long)(lw + 1), (long long)sink);
+  return SPRUCE_OK;
+}
+
+int spruce_gate_select(const float* qp, const float* kp, int64_t B, int64_t G, int64_t qb, int64_t P, int64_t K,
+                       int64_t local_window, int64_t sink_blocks, int32_t* out, const int64_t out_strides[3],
+                       void* stream) {
+  int rc = check_select_policy(K, local_window, sink_blocks);
+  if (rc) return rc;
+  if (B < 0 || G < 1 || qb < 0 || P < 1 || P > 1024) return fail(SPRUCE_ERR_INVALID, "bad selection shape");
+  if (B == 0 || qb == 0) return SPRUCE_OK;
+  if (spruce::select_rows_for((int)qb, (int)P) == 0)
+    return fail(SPRUCE_ERR_UNSUPPORTED, "qb=%lld query blocks exceed the selection kernel's shared memory",
+                (long long)qb);
+  return cuda_status(spruce::launch_select(qp, kp, (int)B, (int)G, (int)qb, (int)P, (int)K, (int)local_window,
+                                           (int)sink_blocks, out, out_strides, as_stream(stream)),
+                     "selection launch");
+}
+
+int64_t spruce_select_workspace_bytes(int64_t B, int64_t Hkv, int64_t T, int64_t D, int64_t P, int dtype) {
+  const int64_t qb = (T + SPRUCE_BLOCK - 1) / SPRUCE_BLOCK;
+  const int64_t rows = B * Hkv * qb;
+  auto up = [](int64_t x) { return (x + 255) / 256 * 256; };
+  return 2 * up(rows * D * elem_size(dtype)) + 2 * up(rows * P * 4);
+}
+
+int spruce_select_blocks(const void* q, const int64_t q_strides[4], const void* k, const int64_t k_strides[4],
+                         int dtype, int64_t B, int64_t Hq, int64_t Hkv, int64_t T, int64_t D, const float* Wq,
+                         const float* Wk, int64_t P, int64_t K, int64_t local_window, int64_t sink_blocks,
+                         int32_t* out, const int64_t out_strides[3], void* workspace, int64_t workspace_bytes,
+                         void* stream) {
+  int rc = check_select_policy(K, local_window, sink_blocks);
+  if (rc) return rc;
+  const int64_t need = spruce_select_workspace_bytes(B, Hkv, T, D, P, dtype);
+  if (workspace_bytes < need)
+    return fail(SPRUCE_ERR_WORKSPACE, "workspace of %lld bytes, need %lld", (long long)workspace_bytes,
+                (long long)need);
+  if (!aligned16(workspace)) return fail(SPRUCE_ERR_INVALID, "workspace must be 16-byte aligned");
+  const int64_t qb = (T + SPRUCE_BLOCK - 1) / SPRUCE_BLOCK;
+  const int64_t rows = B * Hkv * qb;
+  auto up = [](int64_t x) { return (x + 255) / 256 * 256; };
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  void* pooled_q = ws;
+  void* pooled_k = ws + up(rows * D * elem_size(dtype));
+  float* qp = reinterpret_cast<float*>(ws + 2 * up(rows * D * elem_size(dtype)));
+  float* kp = reinterpret_cast<float*>(ws + 2 * up(rows * D * elem_size(dtype)) + up(rows * P * 4));
+  rc = spruce_pool_qk(q, q_strides, k, k_strides, dtype, B, Hq, Hkv, T, D, pooled_q, pooled_k, stream);
+  if (rc) return rc;
+  rc = spruce_gate_project(pooled_q, dtype, rows, D, Wq, P, qp, stream);
+  if (rc) return rc;
+  rc = spruce_gate_project(pooled_k, dtype, rows, D, Wk, P, kp, stream);
+  if (rc) return rc;
+  return spruce_gate_select(qp, kp, B, Hkv, qb, P, K, local_window, sink_blocks, out, out_strides, stream);
+}
+
+int spruce_pack_selected_ids(const int64_t* ids, int64_t R, int64_t qb, int64_t C, int64_t K, int64_t local_window,
+                             int64_t key_blocks, int64_t sink_blocks, int32_t* out, void* stream) {
+  int rc = check_select_policy(K, local_window, sink_blocks);
+  if (rc) return rc;
+  if (key_blocks < 1) return fail(SPRUCE_ERR_INVALID, "key_blocks must be >= 1, got %lld", (long long)key_blocks);
+  if (R < 0 || qb < 0 || C < 0) return fail(SPRUCE_ERR_INVALID, "bad ids shape");
+  const int64_t span = qb > key_blocks ? qb : key_blocks;
+  if (span > (1 << 20)) return fail(SPRUCE_ERR_UNSUPPORTED, "too many blocks (%lld)", (long long)span);
+  return cuda_status(spruce::launch_pack_ids(ids, R, (int)qb, (int)C, (int)K, (int)local_window, (int)key_blocks,
+                                             (int)sink_blocks, out, as_stream(stream)),
+                     "pack launch");
+}
+
+int spruce_validate_selected_blocks(const int32_t* sel, int64_t B, int64_t L, int64_t G, int64_t qb, int64_t K,
+                                    int64_t local_window, int64_t* result, void* stream) {
+  if (local_window < 0) return fail(SPRUCE_ERR_INVALID, "local_window must be >= 0, got %lld", (long long)local_window);
+  if (B < 0 || L < 0 || G < 0 || qb < 0 || K < 0) return fail(SPRUCE_ERR_INVALID, "bad shape");
+  return cuda_status(spruce::launch_validate(sel, B * L * G * qb, (int)qb, (int)K, (int)local_window, result,
+                                             as_stream(stream)),
+                     "validate launch");
+}
+
+int spruce_sparse_attention_fwd(const void* q, const int64_t q_strides[4], const void* k, const int64_t k_strides[4],
+                                const void* v, const int64_t v_strides[4], const int32_t* indices,
+                                const int64_t idx_strides[4], void* out, const int64_t out_strides[4], int dtype,
+                                int64_t B, int64_t Hq, int64_t Hkv, int64_t T, int64_t D, int64_t Kw, float scale,
+                                uint32_t* status, void* stream) {
+  if (!valid_dtype(dtype)) return fail(SPRUCE_ERR_INVALID, "unsupported dtype code %d", dtype);
+  if (D != 64 && D != 128) return fail(SPRUCE_ERR_INVALID, "kernel supports head_dim 64 or 128, got %lld", (long long)D);
+  if (B < 0 || Hq < 1 || Hkv < 1 || T < 0 || Kw < 0) return fail(SPRUCE_ERR_INVALID, "bad attention shape");
+  if (Hq % Hkv) return fail(SPRUCE_ERR_INVALID, "query heads must be divisible by KV heads");
+  if (q_strides[3] != 1 || k_strides[3] != 1 || v_strides[3] != 1 || idx_strides[3] != 1 || out_strides[3] != 1)
+    return fail(SPRUCE_ERR_INVALID, "q, k, v, and indices must have a contiguous final dimension");
+  if (B == 0 || T == 0) return SPRUCE_OK;
+  if (T > (int64_t)1 << 30 || Hq > 65535 || B > 65535)
+    return fail(SPRUCE_ERR_UNSUPPORTED, "shape too large for the launch grid");
+  spruce::AttnArgs a{q, k, v, q_strides, k_strides, v_strides, indices, idx_strides, out, out_strides,
+                     (int)B, (int)Hq, (int)Hkv, (int)T, (int)D, (int)Kw, scale, status};
+  if (dtype == SPRUCE_DTYPE_F32) {
+    if (Kw > 8192) return fail(SPRUCE_ERR_UNSUPPORTED, "row width %lld too large", (long long)Kw);
+    return cuda_status(spruce::launch_attn_f32(a, as_stream(stream)), "fp32 attention launch");
+  }
+  // TMA needs 16-byte aligned bases and strides that are multiples of 16 bytes.
+  const int64_t* ss[3] = {q_strides, k_strides, v_strides};
+  const void* bases[3] = {q, k, v};
+  for (int t = 0; t < 3; ++t) {
+    if (!aligned16(bases[t]) || ss[t][0] % 8 || ss[t][1] % 8 || ss[t][2] % 8)
+      return fail(SPRUCE_ERR_UNSUPPORTED, "q/k/v need 16-byte aligned bases and strides");
+  }
+  if (!aligned16(out) || out_strides[0] % 8 || out_strides[1] % 8 || out_strides[2] % 8)
+    return fail(SPRUCE_ERR_UNSUPPORTED, "out needs 16-byte aligned base and strides");
+  if (Kw > spruce::attn_sm100_max_kw((int)D))
+    return fail(SPRUCE_ERR_UNSUPPORTED, "row width %lld exceeds %d", (long long)Kw, spruce::attn_sm100_max_kw((int)D));
+  return cuda_status(spruce::launch_attn_sm100(a, dtype, as_stream(stream)), "tcgen05 attention launch");
+}
+
+}  // extern "C"

@@ -1,0 +1,59 @@
+// Internal launcher declarations shared by the .cu files and the C ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace spruce {
+
+struct PoolJob {
+  const void* x;       // [B, H, T, D] strided
+  int64_t sb, sh, st;  // element strides (d stride is 1)
+  void* out;           // [B, Hout, nb, D] contiguous
+  int rep;             // heads averaged per output row (1 = plain pooling)
+  int hout;            // output heads
+};
+
+template <typename T>
+cudaError_t launch_pool(PoolJob j0, PoolJob j1, int njobs, int B, int T_len, int D, cudaStream_t stream);
+template <typename T>
+cudaError_t launch_group_avg(const void* x, const int64_t* strides, void* out, int B, int H, int T_len, int D,
+                             int G, cudaStream_t stream);
+template <typename T>
+cudaError_t launch_project(const void* x, int64_t N, int D, const float* W, int P, float* out, cudaStream_t stream);
+
+cudaError_t launch_scores(const float* qp, const float* kp, int64_t R, int qb, int kb, int P, float* out,
+                          cudaStream_t stream);
+int select_rows_for(int qb, int P);
+cudaError_t launch_select(const float* qp, const float* kp, int B, int G, int qb, int P, int K, int lw, int sink,
+                          int32_t* out, const int64_t* out_strides, cudaStream_t stream);
+cudaError_t launch_pack_ids(const int64_t* ids, int64_t R, int qb, int C, int K, int lw, int kb, int sink,
+                            int32_t* out, cudaStream_t stream);
+cudaError_t launch_validate(const int32_t* sel, int64_t rows, int qb, int K, int lw, int64_t* result,
+                            cudaStream_t stream);
+
+struct AttnArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  const int64_t* qs;   // element strides [4]
+  const int64_t* ks;
+  const int64_t* vs;
+  const int32_t* idx;
+  const int64_t* is;
+  void* out;
+  const int64_t* os;   // logical [B, Hq, T, D] strides
+  int B, Hq, Hkv, T, D, Kw;
+  float scale;
+  uint32_t* status;
+};
+
+// tcgen05 path (bf16 / fp16).  Returns cudaErrorInvalidValue for shapes it
+// does not cover (the C ABI checks them first).
+cudaError_t launch_attn_sm100(const AttnArgs& a, int dtype, cudaStream_t stream);
+// CUDA-core fp32 path.
+cudaError_t launch_attn_f32(const AttnArgs& a, cudaStream_t stream);
+// Largest row width the tcgen05 kernel accepts for this head dim.
+int attn_sm100_max_kw(int D);
+
+}  // namespace spruce

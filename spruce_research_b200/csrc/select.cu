@@ -1,0 +1,488 @@
+// Flat-gate selection: projection, scores, masked top-k and packing into
+// selected_blocks rows; plus the reference's id packer and validator.
+//
+// References: selector/gate.py:47-101 (FlatGate, P = 1),
+// scripts/route_overrides.py:187-205 (topk -> selected_ids_to_blocks),
+// scripts/export_selected_blocks.py:80-175 (packing policy),
+// interfaces/validator.py:7-62 (row rules).
+//
+// Every score is a fixed-order fp32 fma chain over the projection dim
+// followed by a true division by sqrt(P), so the CUDA result equals the CPU
+// restatement bit for bit; the top-k is an exact radix select on the
+// order-preserving integer image of the scores with ties broken toward the
+// lowest block id, so indices are bit-exact too.
+#include <algorithm>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace spruce {
+
+// ------------------------------------------------------------------ projection
+constexpr int kProjRows = 8;
+
+template <typename T>
+__global__ void __launch_bounds__(128) project_kernel(const T* __restrict__ x, int64_t N, int D,
+                                                      const float* __restrict__ W, int P, float* __restrict__ out) {
+  extern __shared__ float xs[];  // [kProjRows][D]
+  const int64_t n0 = (int64_t)blockIdx.x * kProjRows;
+  const int rows = (int)(N - n0 < kProjRows ? N - n0 : kProjRows);
+  for (int e = threadIdx.x; e < rows * D; e += blockDim.x) xs[e] = Elem<T>::to_f(x[n0 * D + e]);
+  __syncthreads();
+  for (int p = threadIdx.x; p < P; p += blockDim.x) {
+    float acc[kProjRows];
+#pragma unroll
+    for (int r = 0; r < kProjRows; ++r) acc[r] = 0.0f;
+    for (int d = 0; d < D; ++d) {
+      const float w = __ldg(W + (int64_t)d * P + p);
+#pragma unroll
+      for (int r = 0; r < kProjRows; ++r) acc[r] = __fmaf_rn(xs[r * D + d], w, acc[r]);
+    }
+    for (int r = 0; r < rows; ++r) out[(n0 + r) * P + p] = acc[r];
+  }
+}
+
+// ------------------------------------------------------------------ score tiles
+// A CTA of 256 threads scores ROWS query rows against 256 key columns at a
+// time: thread t owns column j0 + t and keeps ROWS fp32 accumulators; the
+// key projections are staged transposed in shared memory, 32 p at a time.
+constexpr int kScoreThreads = 256;
+constexpr int kPChunk = 32;
+
+__device__ __forceinline__ uint32_t order_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return 0xffffffffu;  // NaN sorts above +inf (torch.topk)
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// qs: [ROWS][P] query projections in smem; kT: [kPChunk][kScoreThreads] staging.
+// Writes fp32 scores of columns [j0, j0 + 256) ∩ [0, ncols) via `emit(r, j, s)`.
+template <int ROWS, typename Emit>
+__device__ __forceinline__ void score_columns(const float* qs, const float* __restrict__ kp, int P, int j0,
+                                              int ncols, float* kT, float denom, Emit emit) {
+  const int t = threadIdx.x;
+  float acc[ROWS];
+#pragma unroll
+  for (int r = 0; r < ROWS; ++r) acc[r] = 0.0f;
+  for (int p0 = 0; p0 < P; p0 += kPChunk) {
+    __syncthreads();
+    // Stage kp[j0 .. j0+255][p0 .. p0+31] transposed: coalesced along p.
+    for (int e = t; e < kPChunk * kScoreThreads; e += kScoreThreads) {
+      const int jj = e / kPChunk;
+      const int pp = e % kPChunk;
+      const int j = j0 + jj;
+      kT[pp * kScoreThreads + jj] = (j < ncols && p0 + pp < P) ? __ldg(kp + (int64_t)j * P + p0 + pp) : 0.0f;
+    }
+    __syncthreads();
+    const int pn = min(kPChunk, P - p0);
+    for (int pp = 0; pp < pn; ++pp) {
+      const float kv = kT[pp * kScoreThreads + t];
+#pragma unroll
+      for (int r = 0; r < ROWS; ++r) acc[r] = __fmaf_rn(qs[r * P + p0 + pp], kv, acc[r]);
+    }
+  }
+  const int j = j0 + t;
+  if (j < ncols) {
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) emit(r, j, __fdiv_rn(acc[r], denom));
+  }
+}
+
+// Full score matrix (FlatGate.forward, P = 1): grid (ceil(qb/ROWS), R).
+template <int ROWS>
+__global__ void __launch_bounds__(kScoreThreads) scores_kernel(const float* __restrict__ qp,
+                                                               const float* __restrict__ kp, int qb, int kb, int P,
+                                                               float* __restrict__ out, float denom) {
+  extern __shared__ float sm[];
+  float* qs = sm;                   // [ROWS][P]
+  float* kT = sm + ROWS * P;        // [kPChunk][256]
+  const int r0 = blockIdx.x * ROWS;
+  const int64_t mat = blockIdx.y;
+  const float* q = qp + mat * qb * P;
+  const float* k = kp + mat * kb * P;
+  for (int e = threadIdx.x; e < ROWS * P; e += kScoreThreads) {
+    const int r = e / P;
+    qs[e] = (r0 + r < qb) ? q[(int64_t)(r0 + r) * P + e % P] : 0.0f;
+  }
+  for (int j0 = 0; j0 < kb; j0 += kScoreThreads) {
+    score_columns<ROWS>(qs, k, P, j0, kb, kT, denom, [&](int r, int j, float s) {
+      if (r0 + r < qb) out[(mat * qb + r0 + r) * kb + j] = s;
+    });
+  }
+}
+
+// ------------------------------------------------------------------ fused select
+struct SelectArgs {
+  const float* qp;   // [B, G, qb, P]
+  const float* kp;   // [B, G, qb, P]
+  int B, G, qb, P, K, local_window, sink, W;
+  int32_t* out;
+  int64_t osb, osg, osq;
+  float denom;
+};
+
+// Radix select of the k-th largest key among keys[lo, hi) (k >= 1, k <= hi-lo)
+// by one warp.  Returns the threshold key; *need = how many keys equal to the
+// threshold belong to the top k (taken lowest index first).
+__device__ __forceinline__ uint32_t warp_radix_select(const uint32_t* keys, int lo, int hi, int k, int* hist,
+                                                      int* need) {
+  const int lane = threadIdx.x & 31;
+  uint32_t prefix = 0, pmask = 0;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int b = lane; b < 256; b += 32) hist[b] = 0;
+    __syncwarp();
+    for (int j = lo + lane; j < hi; j += 32) {
+      const uint32_t key = keys[j];
+      if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1);
+    }
+    __syncwarp();
+    int local = 0;
+#pragma unroll
+    for (int b = 0; b < 8; ++b) local += hist[lane * 8 + b];
+    // Suffix sums over lanes: S_l = sum_{l' >= l} local_{l'}.
+    int suffix = local;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int v = __shfl_down_sync(0xffffffffu, suffix, off);
+      if (lane + off < 32) suffix += v;
+    }
+    const unsigned ge = __ballot_sync(0xffffffffu, suffix >= k);
+    const int hl = 31 - __clz(ge);  // highest lane whose suffix reaches k
+    int digit = 0, above = 0;
+    if (lane == hl) {
+      above = suffix - local;
+      for (int b = 7; b >= 0; --b) {
+        const int c = hist[lane * 8 + b];
+        if (above + c >= k) { digit = lane * 8 + b; break; }
+        above += c;
+      }
+    }
+    digit = __shfl_sync(0xffffffffu, digit, hl);
+    above = __shfl_sync(0xffffffffu, above, hl);
+    prefix |= static_cast<uint32_t>(digit) << shift;
+    pmask |= 0xFFu << shift;
+    k -= above;
+    __syncwarp();
+  }
+  *need = k;
+  return prefix;
+}
+
+template <int ROWS>
+__global__ void __launch_bounds__(kScoreThreads) select_kernel(SelectArgs a) {
+  extern __shared__ float sm[];
+  const int P = a.P;
+  const int qb = a.qb;
+  float* qs = sm;                                   // [ROWS][P]
+  float* kT = qs + ROWS * P;                        // [kPChunk][256]
+  int* hist = reinterpret_cast<int*>(kT + kPChunk * kScoreThreads);  // [8 warps][256]
+  uint32_t* keys = reinterpret_cast<uint32_t*>(hist + 8 * 256);     // [ROWS][qb]
+
+  const int tiles = (qb + ROWS - 1) / ROWS;
+  const int tile = tiles - 1 - blockIdx.x;          // heavy (late) rows first
+  const int g = blockIdx.y, b = blockIdx.z;
+  const int r0 = tile * ROWS;
+  const int64_t mat = (int64_t)b * a.G + g;
+  const float* q = a.qp + mat * qb * P;
+  const float* k = a.kp + mat * qb * P;
+  for (int e = threadIdx.x; e < ROWS * P; e += kScoreThreads) {
+    const int r = e / P;
+    qs[e] = (r0 + r < qb) ? q[(int64_t)(r0 + r) * P + e % P] : 0.0f;
+  }
+  // Only candidates j < q - local_window of the tile's last row are needed.
+  const int ncols = max(0, min(qb, r0 + ROWS - a.local_window));
+  for (int j0 = 0; j0 < ncols; j0 += kScoreThreads) {
+    score_columns<ROWS>(qs, k, P, j0, ncols, kT, a.denom,
+                        [&](int r, int j, float s) { keys[r * qb + j] = order_key(s); });
+  }
+  __syncthreads();
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int r = warp; r < ROWS; r += kScoreThreads / 32) {
+    const int i = r0 + r;
+    if (i >= qb) break;
+    const uint32_t* kr = keys + r * qb;
+    const int lo = a.sink;
+    const int hi = min(qb, i - a.local_window);
+    const int n = max(0, hi - lo);
+    uint32_t thr = 0;
+    int need = 0;
+    const bool partial = n > a.W;  // more candidates than free slots: top-W only
+    if (partial && a.W > 0) thr = warp_radix_select(kr, lo, hi, a.W, hist + warp * 256, &need);
+    int32_t* o = a.out + b * a.osb + g * a.osg + (int64_t)i * a.osq;
+    int pos = 0, ties = 0;
+    for (int j0 = 0; j0 <= i; j0 += 32) {
+      const int j = j0 + lane;
+      bool keep = false;
+      bool tie = false;
+      if (j <= i) {
+        const bool sink = j < a.sink && j < i - a.local_window;
+        const bool local = j >= i - a.local_window;
+        bool cand = false;
+        if (j >= lo && j < hi) {
+          if (!partial) cand = true;
+          else if (a.W > 0) {
+            const uint32_t key = kr[j];
+            cand = key > thr;
+            tie = key == thr;
+          }
+        }
+        keep = sink || local || cand;
+      }
+      const unsigned tmask = __ballot_sync(0xffffffffu, tie);
+      if (tie) keep = (ties + __popc(tmask & ((1u << lane) - 1u))) < need;
+      ties += __popc(tmask);
+      const unsigned kmask = __ballot_sync(0xffffffffu, keep);
+      const int slot = pos + __popc(kmask & ((1u << lane) - 1u));
+      if (keep && slot < a.K) o[slot] = j;
+      pos += __popc(kmask);
+    }
+    for (int s = pos + lane; s < a.K; s += 32) o[s] = -1;
+  }
+}
+
+// ------------------------------------------------------------------ id packing
+struct PackArgs {
+  const int64_t* ids;
+  int64_t R;
+  int qb, C, K, lw, kb, sink, words;
+  int32_t* out;
+};
+
+__global__ void __launch_bounds__(256) pack_ids_kernel(PackArgs a) {
+  extern __shared__ uint32_t bm_all[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + warp;
+  if (row >= a.R * a.qb) return;
+  uint32_t* bm = bm_all + warp * a.words;
+  const int q = row % a.qb;
+  for (int w = lane; w < a.words; w += 32) bm[w] = 0;
+  __syncwarp();
+  const int64_t* r = a.ids + row * a.C;
+  for (int c = lane; c < a.C; c += 32) {
+    const int64_t id = r[c];
+    if (id >= 0 && id < a.kb && id <= q && id < q - a.lw && id >= a.sink)
+      atomicOr(&bm[id >> 5], 1u << (id & 31));
+  }
+  __syncwarp();
+  const int local_count = min(q + 1, a.lw + 1);
+  const int sink_count = min(max(q - a.lw, 0), a.sink);
+  const int remaining = a.K - local_count - sink_count;
+  // Keep only the `remaining` smallest marked ids.
+  int running = 0;
+  for (int w0 = 0; w0 < a.words; w0 += 32) {
+    const int w = w0 + lane;
+    uint32_t bits = w < a.words ? bm[w] : 0u;
+    const int cnt = __popc(bits);
+    int incl = cnt;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += v;
+    }
+    const int start = running + incl - cnt;
+    if (start >= remaining) bits = 0u;
+    else
+      for (int extra = start + cnt - remaining; extra > 0; --extra) bits &= ~(1u << (31 - __clz(bits)));
+    if (w < a.words) bm[w] = bits;
+    running += __shfl_sync(0xffffffffu, incl, 31);
+  }
+  __syncwarp();
+  // Forced sink ids (strictly before the local window) and the local window.
+  for (int j = lane; j < a.sink; j += 32)
+    if (j < q - a.lw) atomicOr(&bm[j >> 5], 1u << (j & 31));
+  for (int j = max(0, q - a.lw) + lane; j <= q; j += 32) atomicOr(&bm[j >> 5], 1u << (j & 31));
+  __syncwarp();
+  int32_t* o = a.out + row * a.K;
+  int pos = 0;
+  for (int w0 = 0; w0 < a.words; w0 += 32) {
+    const int w = w0 + lane;
+    uint32_t bits = w < a.words ? bm[w] : 0u;
+    const int cnt = __popc(bits);
+    int incl = cnt;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += v;
+    }
+    int slot = pos + incl - cnt;
+    while (bits) {
+      const int bit = __ffs(bits) - 1;
+      bits &= bits - 1u;
+      if (slot < a.K) o[slot] = w * 32 + bit;
+      ++slot;
+    }
+    pos += __shfl_sync(0xffffffffu, incl, 31);
+  }
+  for (int s = pos + lane; s < a.K; s += 32) o[s] = -1;
+}
+
+// ------------------------------------------------------------------ validator
+__global__ void validate_init_kernel(unsigned long long* result) { *result = 0xFFFFFFFFFFFFFFFFull; }
+
+__global__ void __launch_bounds__(256) validate_kernel(const int32_t* __restrict__ sel, int64_t rows, int qb, int K,
+                                                       int lw, unsigned long long* result) {
+  const int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= rows) return;
+  const int q = row % qb;
+  const int32_t* r = sel + row * K;
+  int rule = 0;
+  // 1: causal (every real id <= q); real ids are the values != -1.
+  for (int c = 0; c < K && !rule; ++c)
+    if (r[c] != -1 && r[c] > q) rule = 1;
+  // 2: sorted (non-decreasing among real ids); 3: no duplicates.
+  if (!rule) {
+    int prev = 0;
+    bool have = false;
+    for (int c = 0; c < K; ++c) {
+      if (r[c] == -1) continue;
+      if (have && r[c] < prev) { rule = 2; break; }
+      prev = r[c];
+      have = true;
+    }
+  }
+  if (!rule) {
+    int prev = 0;
+    bool have = false;
+    for (int c = 0; c < K; ++c) {
+      if (r[c] == -1) continue;
+      if (have && r[c] == prev) { rule = 3; break; }
+      prev = r[c];
+      have = true;
+    }
+  }
+  // 4: local window blocks max(0, q - lw) .. q present.
+  if (!rule) {
+    for (int need = max(0, q - lw); need <= q && !rule; ++need) {
+      bool found = false;
+      for (int c = 0; c < K; ++c)
+        if (r[c] == need) { found = true; break; }
+      if (!found) rule = 4;
+    }
+  }
+  // 5: padding only after all real ids.
+  if (!rule) {
+    bool pad = false;
+    for (int c = 0; c < K; ++c) {
+      if (r[c] == -1) pad = true;
+      else if (pad) { rule = 5; break; }
+    }
+  }
+  if (rule) atomicMin(result, static_cast<unsigned long long>(row) * 8ull + rule);
+}
+
+__global__ void validate_finish_kernel(unsigned long long* result) {
+  if (*result == 0xFFFFFFFFFFFFFFFFull) *reinterpret_cast<long long*>(result) = -1;
+}
+
+// ------------------------------------------------------------------ launchers
+template <typename T>
+cudaError_t launch_project(const void* x, int64_t N, int D, const float* W, int P, float* out,
+                           cudaStream_t stream) {
+  if (N == 0) return cudaSuccess;
+  const int grid = (int)((N + kProjRows - 1) / kProjRows);
+  const size_t smem = sizeof(float) * kProjRows * D;
+  project_kernel<T><<<grid, 128, smem, stream>>>(static_cast<const T*>(x), N, D, W, P, out);
+  return cudaGetLastError();
+}
+template cudaError_t launch_project<float>(const void*, int64_t, int, const float*, int, float*, cudaStream_t);
+template cudaError_t launch_project<__nv_bfloat16>(const void*, int64_t, int, const float*, int, float*,
+                                                   cudaStream_t);
+template cudaError_t launch_project<__half>(const void*, int64_t, int, const float*, int, float*, cudaStream_t);
+
+static float gate_denom(int P) { return static_cast<float>(std::sqrt(static_cast<double>(P))); }
+
+cudaError_t launch_scores(const float* qp, const float* kp, int64_t R, int qb, int kb, int P, float* out,
+                          cudaStream_t stream) {
+  constexpr int ROWS = 16;
+  const size_t smem = sizeof(float) * (ROWS * P + kPChunk * kScoreThreads);
+  cudaError_t e = cudaFuncSetAttribute(scores_kernel<ROWS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid((qb + ROWS - 1) / ROWS, (unsigned)R);
+  scores_kernel<ROWS><<<grid, kScoreThreads, smem, stream>>>(qp, kp, qb, kb, P, out, gate_denom(P));
+  return cudaGetLastError();
+}
+
+size_t select_smem_bytes(int rows, int qb, int P) {
+  return sizeof(float) * (rows * P + kPChunk * kScoreThreads) + sizeof(int) * 8 * 256 +
+         sizeof(uint32_t) * (size_t)rows * qb;
+}
+
+template <int ROWS>
+static cudaError_t launch_select_rows(const SelectArgs& a, cudaStream_t stream) {
+  const size_t smem = select_smem_bytes(ROWS, a.qb, a.P);
+  cudaError_t e = cudaFuncSetAttribute(select_kernel<ROWS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid((a.qb + ROWS - 1) / ROWS, a.G, a.B);
+  select_kernel<ROWS><<<grid, kScoreThreads, smem, stream>>>(a);
+  return cudaGetLastError();
+}
+
+int select_rows_for(int qb, int P) {
+  const size_t limit = 200 * 1024;
+  if (select_smem_bytes(16, qb, P) <= limit) return 16;
+  if (select_smem_bytes(8, qb, P) <= limit) return 8;
+  if (select_smem_bytes(4, qb, P) <= limit) return 4;
+  return 0;
+}
+
+cudaError_t launch_select(const float* qp, const float* kp, int B, int G, int qb, int P, int K, int lw, int sink,
+                          int32_t* out, const int64_t* out_strides, cudaStream_t stream) {
+  SelectArgs a;
+  a.qp = qp;
+  a.kp = kp;
+  a.B = B;
+  a.G = G;
+  a.qb = qb;
+  a.P = P;
+  a.K = K;
+  a.local_window = lw;
+  a.sink = std::min(sink, qb);
+  a.W = std::min(K - (lw + 1) - sink, qb);
+  a.out = out;
+  a.osb = out_strides[0];
+  a.osg = out_strides[1];
+  a.osq = out_strides[2];
+  a.denom = gate_denom(P);
+  switch (select_rows_for(qb, P)) {
+    case 16: return launch_select_rows<16>(a, stream);
+    case 8: return launch_select_rows<8>(a, stream);
+    case 4: return launch_select_rows<4>(a, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_pack_ids(const int64_t* ids, int64_t R, int qb, int C, int K, int lw, int kb, int sink,
+                            int32_t* out, cudaStream_t stream) {
+  PackArgs a;
+  a.ids = ids;
+  a.R = R;
+  a.qb = qb;
+  a.C = C;
+  a.K = K;
+  a.lw = lw;
+  a.kb = kb;
+  a.sink = std::min(sink, kb);
+  a.words = (std::max(qb, kb) + 31) / 32;
+  a.out = out;
+  const int64_t rows = R * qb;
+  if (rows == 0) return cudaSuccess;
+  const size_t smem = sizeof(uint32_t) * 8 * a.words;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(pack_ids_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  pack_ids_kernel<<<(unsigned)((rows + 7) / 8), 256, smem, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_validate(const int32_t* sel, int64_t rows, int qb, int K, int lw, int64_t* result,
+                            cudaStream_t stream) {
+  auto* res = reinterpret_cast<unsigned long long*>(result);
+  validate_init_kernel<<<1, 1, 0, stream>>>(res);
+  if (rows > 0) validate_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, stream>>>(sel, rows, qb, K, lw, res);
+  validate_finish_kernel<<<1, 1, 0, stream>>>(res);
+  return cudaGetLastError();
+}
+
+}  // namespace spruce

@@ -1,0 +1,223 @@
+"""Typed torch front end of the C ABI: one function per extern "C" entry point.
+
+Each function takes CUDA tensors, checks dtypes/shapes the way the reference
+does, allocates outputs on the input's device through torch's caching
+allocator, and enqueues the kernel on the current stream.  The reference-named
+drop-ins (FlatGate, _proto_pool_seq, direct_index_sparse_triton, ...) are thin
+layers over these.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+
+BLOCK = 64
+
+
+def _dt(t: torch.Tensor) -> int:
+    try:
+        return _lib.DTYPE_CODE[t.dtype]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {t.dtype}; expected float32, bfloat16 or float16") from None
+
+
+def _vec_ok(t: torch.Tensor) -> torch.Tensor:
+    """A view the 16-byte vector kernels accept (copy only if it is not)."""
+    es = t.element_size()
+    vn = 16 // es
+    if t.stride(-1) == 1 and t.data_ptr() % 16 == 0 and all(s % vn == 0 for s in t.stride()[:-1]):
+        return t
+    return t.contiguous()
+
+
+def group_avg_tokens(x: torch.Tensor, G: int) -> torch.Tensor:
+    """[b, H, L, d] -> [b, G, L, d] (teacher/chunked_extract.py:75-80)."""
+    _lib.require_cuda(x)
+    b, H, T, d = x.shape
+    if H % G:
+        raise AssertionError(f"H={H} not divisible by G={G}")
+    x = _vec_ok(x)
+    out = torch.empty((b, G, T, d), device=x.device, dtype=x.dtype)
+    L = _lib.load()
+    _lib.check(L.spruce_group_avg_tokens(x.data_ptr(), _lib.strides(x), _dt(x), b, H, T, d, G, out.data_ptr(),
+                                         _lib.stream_of(x)))
+    return out
+
+
+def proto_pool(x: torch.Tensor, block: int = BLOCK, P: int = 1) -> torch.Tensor:
+    """[b, H, L, d] -> [b, H, nb, P, d] (teacher/chunked_extract.py:27-72)."""
+    _lib.require_cuda(x)
+    b, H, T, d = x.shape
+    nb = (T + block - 1) // block
+    x = _vec_ok(x)
+    out = torch.empty((b, H, nb, P, d), device=x.device, dtype=x.dtype)
+    L = _lib.load()
+    _lib.check(L.spruce_proto_pool(x.data_ptr(), _lib.strides(x), _dt(x), b, H, T, d, block, P, out.data_ptr(),
+                                   _lib.stream_of(x)))
+    return out
+
+
+def pool_qk(q: torch.Tensor, k: torch.Tensor):
+    """Selector inputs: (pooled_q, pooled_k), each [B, Hkv, qb, d] in the input dtype."""
+    _lib.require_cuda(q, k)
+    B, Hq, T, d = q.shape
+    Hkv = k.shape[1]
+    if q.dtype != k.dtype:
+        raise ValueError("q and k must share a dtype")
+    q, k = _vec_ok(q), _vec_ok(k)
+    qb = (T + BLOCK - 1) // BLOCK
+    pq = torch.empty((B, Hkv, qb, d), device=q.device, dtype=q.dtype)
+    pk = torch.empty((B, Hkv, qb, d), device=q.device, dtype=q.dtype)
+    L = _lib.load()
+    _lib.check(L.spruce_pool_qk(q.data_ptr(), _lib.strides(q), k.data_ptr(), _lib.strides(k), _dt(q), B, Hq, Hkv, T,
+                                d, pq.data_ptr(), pk.data_ptr(), _lib.stream_of(q)))
+    return pq, pk
+
+
+def gate_project(x: torch.Tensor, W: torch.Tensor) -> torch.Tensor:
+    """fp32(x[..., d]) @ W[d, p] with a fixed fma order -> fp32 [..., p]."""
+    _lib.require_cuda(x, W)
+    d, p = W.shape
+    if x.shape[-1] != d:
+        raise ValueError(f"feature dim {x.shape[-1]} does not match projection {tuple(W.shape)}")
+    xc = x.contiguous()
+    Wc = W.detach().float().contiguous()
+    out = torch.empty((*x.shape[:-1], p), device=x.device, dtype=torch.float32)
+    N = xc.numel() // d if d else 0
+    L = _lib.load()
+    _lib.check(L.spruce_gate_project(xc.data_ptr(), _dt(xc), N, d, Wc.data_ptr(), p, out.data_ptr(),
+                                     _lib.stream_of(x)))
+    return out
+
+
+def gate_scores(qp: torch.Tensor, kp: torch.Tensor) -> torch.Tensor:
+    """qp [R, qb, p], kp [R, kb, p] fp32 -> [R, qb, kb] = qp.kp / sqrt(p)."""
+    _lib.require_cuda(qp, kp)
+    R, qb, p = qp.shape
+    kb = kp.shape[1]
+    qp = qp.float().contiguous()
+    kp = kp.float().contiguous()
+    out = torch.empty((R, qb, kb), device=qp.device, dtype=torch.float32)
+    L = _lib.load()
+    _lib.check(L.spruce_gate_scores(qp.data_ptr(), kp.data_ptr(), R, qb, kb, p, out.data_ptr(), _lib.stream_of(qp)))
+    return out
+
+
+def gate_select(qp: torch.Tensor, kp: torch.Tensor, k_selected: int, local_window: int = 0, sink_blocks: int = 1,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """qp/kp [B, G, qb, p] fp32 -> selected rows int32 [B, G, qb, K] (or into `out`)."""
+    _lib.require_cuda(qp, kp)
+    B, G, qb, p = qp.shape
+    qp = qp.float().contiguous()
+    kp = kp.float().contiguous()
+    if out is None:
+        out = torch.empty((B, G, qb, k_selected), device=qp.device, dtype=torch.int32)
+    _check_rows_out(out, B, G, qb, k_selected)
+    L = _lib.load()
+    _lib.check(L.spruce_gate_select(qp.data_ptr(), kp.data_ptr(), B, G, qb, p, k_selected, local_window, sink_blocks,
+                                    out.data_ptr(), _lib.int64s(*out.stride()[:3]), _lib.stream_of(qp)))
+    return out
+
+
+def _check_rows_out(out: torch.Tensor, B: int, G: int, qb: int, K: int) -> None:
+    if out.dtype != torch.int32 or tuple(out.shape) != (B, G, qb, K) or out.stride(-1) != 1:
+        raise ValueError(f"selected rows must be int32 [{B}, {G}, {qb}, {K}] with a unit last stride")
+
+
+def select_workspace_bytes(q: torch.Tensor, k: torch.Tensor, proj_dim: int) -> int:
+    B, _, T, d = q.shape
+    return int(_lib.load().spruce_select_workspace_bytes(B, k.shape[1], T, d, proj_dim, _dt(q)))
+
+
+def select_blocks(q: torch.Tensor, k: torch.Tensor, Wq: torch.Tensor, Wk: torch.Tensor, k_selected: int,
+                  local_window: int = 0, sink_blocks: int = 1, out: torch.Tensor | None = None,
+                  workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Whole flat selector of one layer: int32 rows [B, Hkv, qb, K] (or into `out`)."""
+    _lib.require_cuda(q, k, Wq, Wk)
+    B, Hq, T, d = q.shape
+    Hkv = k.shape[1]
+    p = Wq.shape[1]
+    if q.dtype != k.dtype:
+        raise ValueError("q and k must share a dtype")
+    if tuple(Wq.shape) != (d, p) or tuple(Wk.shape) != (d, p):
+        raise ValueError(f"gate weights must be [{d}, p]")
+    q, k = _vec_ok(q), _vec_ok(k)
+    Wq = Wq.detach().float().contiguous()
+    Wk = Wk.detach().float().contiguous()
+    qb = (T + BLOCK - 1) // BLOCK
+    if out is None:
+        out = torch.empty((B, Hkv, qb, k_selected), device=q.device, dtype=torch.int32)
+    _check_rows_out(out, B, Hkv, qb, k_selected)
+    need = select_workspace_bytes(q, k, p)
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(max(need, 16), device=q.device, dtype=torch.uint8)
+    L = _lib.load()
+    _lib.check(L.spruce_select_blocks(q.data_ptr(), _lib.strides(q), k.data_ptr(), _lib.strides(k), _dt(q), B, Hq,
+                                      Hkv, T, d, Wq.data_ptr(), Wk.data_ptr(), p, k_selected, local_window,
+                                      sink_blocks, out.data_ptr(), _lib.int64s(*out.stride()[:3]),
+                                      workspace.data_ptr(), workspace.numel() * workspace.element_size(),
+                                      _lib.stream_of(q)))
+    return out
+
+
+def pack_selected_ids(ids: torch.Tensor, k_selected: int, local_window: int, key_blocks: int,
+                      sink_blocks: int) -> torch.Tensor:
+    """ids [R, qb, C] (any int dtype) -> int32 [R, qb, K] with the reference packing policy."""
+    _lib.require_cuda(ids)
+    R, qb, C = ids.shape
+    ids64 = ids.to(torch.int64).contiguous()
+    out = torch.empty((R, qb, k_selected), device=ids.device, dtype=torch.int32)
+    L = _lib.load()
+    _lib.check(L.spruce_pack_selected_ids(ids64.data_ptr(), R, qb, C, k_selected, local_window, key_blocks,
+                                          sink_blocks, out.data_ptr(), _lib.stream_of(ids)))
+    return out
+
+
+def validate_first_violation(sel: torch.Tensor, local_window: int) -> tuple[int, int] | None:
+    """(flat row, rule) of the first violating row of int32 [B, L, G, qb, K], or None."""
+    _lib.require_cuda(sel)
+    B, Ln, G, qb, K = sel.shape
+    s = sel.contiguous()
+    res = torch.empty(1, device=sel.device, dtype=torch.int64)
+    L = _lib.load()
+    _lib.check(L.spruce_validate_selected_blocks(s.data_ptr(), B, Ln, G, qb, K, local_window, res.data_ptr(),
+                                                 _lib.stream_of(sel)))
+    v = int(res.item())
+    if v < 0:
+        return None
+    return v // 8, v % 8
+
+
+def sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices: torch.Tensor,
+                     scale: float | None = None, out: torch.Tensor | None = None,
+                     status: torch.Tensor | None = None) -> torch.Tensor:
+    """Block-sparse causal GQA attention -> token-major [B, T, Hq, D].
+
+    q [B, Hq, T, D], k/v [B, Hkv, T, D] (strided views are fine),
+    indices int32 [B, Hkv, ceil(T/64), K].
+    """
+    _lib.require_cuda(q, k, v, indices)
+    B, Hq, T, D = q.shape
+    Hkv = k.shape[1]
+    if scale is None:
+        scale = D ** -0.5
+    if not (q.dtype == k.dtype == v.dtype):
+        raise ValueError("q, k and v must share a dtype")
+    if indices.dtype != torch.int32:
+        raise ValueError("indices must be int32 [B,Hkv,ceil(T/64),K]")
+    if out is None:
+        out = torch.empty((B, T, Hq, D), device=q.device, dtype=q.dtype)
+    ostr = _lib.int64s(out.stride(0), out.stride(2), out.stride(1), out.stride(3))
+    L = _lib.load()
+    _lib.check(L.spruce_sparse_attention_fwd(
+        q.data_ptr(), _lib.strides(q), k.data_ptr(), _lib.strides(k), v.data_ptr(), _lib.strides(v),
+        indices.data_ptr(), _lib.strides(indices), out.data_ptr(), ostr, _dt(q), B, Hq, Hkv, T, D,
+        indices.shape[-1], float(scale), status.data_ptr() if status is not None else None, _lib.stream_of(q)))
+    return out
+
+
+def gate_denominator(proj_dim: int) -> float:
+    return float(math.sqrt(proj_dim))

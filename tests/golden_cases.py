@@ -1,0 +1,67 @@
+"""Load the golden fixtures made by tests/golden/make_golden.py (reference outputs)."""
+from __future__ import annotations
+
+import os
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from spruce_research_b200.synthetic import LayerShape, make_gate_weights, make_layer_inputs
+
+HERE = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+DT = {0: torch.float32, 1: torch.bfloat16, 2: torch.float16}
+CASE_NAMES = ["c0", "c1_small", "c1_8k", "ragged_bf16", "gqa_fp16", "batch2_f32"]
+
+
+def from_raw(a: np.ndarray, dtype: torch.dtype) -> torch.Tensor:
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    return t.view(dtype) if dtype in (torch.bfloat16, torch.float16) else t
+
+
+@dataclass
+class GoldenCase:
+    name: str
+    shape: LayerShape
+    dtype: torch.dtype
+    seed: int
+    rope: float | None
+    K: int
+    local_window: int
+    sink: int
+    z: dict
+
+    def inputs(self, device="cpu"):
+        q, k, v = make_layer_inputs(self.shape, self.dtype, self.seed, rope_theta=self.rope)
+        cs = np.array([q.double().sum().item(), k.double().sum().item(), v.double().sum().item()])
+        assert np.allclose(cs, self.z["checksum"], rtol=1e-12, atol=1e-6), "synthetic generator drifted"
+        wq, wk = make_gate_weights(1, self.shape.head_dim, self.shape.head_dim, self.seed + 1000)
+        if device != "cpu":
+            # keep the reference's strided [B, H, T, D] views of token-major storage
+            q = q.transpose(1, 2).contiguous().to(device).transpose(1, 2)
+            k = k.transpose(1, 2).contiguous().to(device).transpose(1, 2)
+            v = v.transpose(1, 2).contiguous().to(device).transpose(1, 2)
+            wq, wk = wq.to(device), wk.to(device)
+        return q, k, v, wq[0], wk[0]
+
+    def golden(self, key: str) -> torch.Tensor:
+        if key in ("pooled_q", "pooled_k", "out"):
+            return from_raw(self.z[key], self.dtype)
+        return torch.from_numpy(np.ascontiguousarray(self.z[key]))
+
+    def out_rows(self) -> torch.Tensor:
+        T = self.shape.tokens
+        return torch.cat([torch.arange(b * 64, min((b + 1) * 64, T)) for b in self.z["out_blocks"]])
+
+
+def load_case(name: str) -> GoldenCase:
+    z = dict(np.load(os.path.join(HERE, f"{name}.npz")))
+    B, Hq, Hkv, T, D = (int(x) for x in z["shape"])
+    K, lw, sink = (int(x) for x in z["policy"])
+    rope = float(z["rope"][0]) or None
+    return GoldenCase(name, LayerShape(B, Hq, Hkv, T, D), DT[int(z["dtype"][0])], int(z["seed"][0]), rope,
+                      K, lw, sink, z)
+
+
+def load_npz(name: str) -> dict:
+    return dict(np.load(os.path.join(HERE, f"{name}.npz")))
