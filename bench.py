@@ -1,0 +1,426 @@
+#!/usr/bin/env python
+"""Benchmark of the SPRUCE sparse-prefill layer on B200.
+
+One step = the whole hot path of one 28Q/4KV-head, d=128, bf16 attention
+layer at 131072 tokens and 10% block density (K=106): block-mean pooling of
+Q and K, FlatGate scores, masked top-k packed into selected_blocks, and causal
+GQA block-sparse attention over the selected tiles.  With N GPUs (torchrun)
+the layer is sharded by KV group (N=2, 4) or half group (N=8) and the outputs
+are all-gathered over NCCL; total work is fixed, so scaling is strong.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+`value` is effective TFLOP/s of the selected tiles (algorithmic FLOPs of the
+step / device time of the step, max over ranks); `e2e` is the same metric
+with the inputs copied from pinned host memory and the output copied back
+inside the timed region; `--impl reference` times the CPU restatement of the
+reference path (the oracle port) on a bounded sample of the same workload.
+Inputs are synthetic (seeded N(0,1) with RoPE and planted affinity) and
+larger than L2 (Q alone is 0.94 GB), so no L2 flush is needed.
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import io
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "sparse-prefill ms/layer & effective TFLOP/s at 128K, 10% density, 1/2/4/8 B200"
+PEAKS_FILE = os.path.join(ROOT, "MEASURED_PEAKS.json")
+TRAFFIC_FILE = os.path.join(ROOT, "profiles", "attn_fwd_sm100_c2.md")
+FALLBACK_PEAK_TFLOPS = 1590.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--tokens", type=int, default=131072)
+    ap.add_argument("--density", type=float, default=0.10)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target length of one CPU sample")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.device_index = device_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader",
+                 "-lms", "200", "-f", self.path], stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = []
+        try:
+            with open(self.path) as f:
+                for r in csv.reader(io.StringIO(f.read())):
+                    if len(r) >= 9:
+                        rows.append([c.strip() for c in r])
+            os.unlink(self.path)
+        except OSError:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+
+        def mhz(s):
+            try:
+                return float(s.split()[0])
+            except (ValueError, IndexError):
+                return None
+
+        sm = [mhz(r[1]) for r in rows if mhz(r[1]) is not None]
+        loaded = [x for x in sm if x > 500] or sm
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[k] for r in rows for k in range(4) if r[5 + k].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": mhz(rows[0][2]), "reasons": reasons, "samples": len(rows)}
+
+
+# ----------------------------------------------------------------- helpers
+def measured_peak():
+    try:
+        with open(PEAKS_FILE) as f:
+            peaks = json.load(f)
+        return float(peaks["bf16_tflops_sustained"]), "measured bf16_tflops_sustained (MEASURED_PEAKS.json)"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_PEAK_TFLOPS, "fallback 1.59 PFLOP/s (no MEASURED_PEAKS.json)"
+
+
+def profiled_traffic(tokens: int):
+    """DRAM bytes per attention launch from the committed ncu summary, scaled to `tokens`."""
+    try:
+        with open(TRAFFIC_FILE) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_c2_launch:"):
+                    b = float(line.split(":", 1)[1].split()[0])
+                    return b if tokens == 131072 else None
+    except (OSError, ValueError):
+        pass
+    return None
+
+
+def workload(args):
+    from spruce_research_b200.synthetic import LayerShape, causal_block_entries, k_for_density, sparse_attention_flops
+
+    shape = LayerShape(1, 28, 4, args.tokens, 128)
+    K = k_for_density(shape.query_blocks, args.density)
+    entries = causal_block_entries(shape.query_blocks, K)
+    flops = sparse_attention_flops(shape, entries)
+    return shape, K, entries, flops
+
+
+def config_dict(args, shape, K, entries, world):
+    par = {1: "single GPU", 2: "kv-group x2", 4: "kv-group x4", 8: "half kv-group x8"}.get(world, f"x{world}")
+    return {
+        "workload": (f"config 2: one Qwen2.5-7B-shaped attention layer, {shape.tokens} tokens, "
+                     f"{shape.q_heads}Q/{shape.kv_heads}KV heads, d={shape.head_dim}, bf16, "
+                     f"{args.density:.0%} block density (K={K}), selector + block-sparse attention"),
+        "tokens": shape.tokens, "q_heads": shape.q_heads, "kv_heads": shape.kv_heads, "head_dim": shape.head_dim,
+        "block": 64, "k_selected": K, "entries_per_kv_group": entries, "parallelism": par,
+        "l2": "inputs larger than L2 (Q 0.94 GB, K/V 0.13 GB each); no flush",
+    }
+
+
+def shard_flops(shape, K, shard) -> float:
+    """Algorithmic FLOPs of this rank's attention launch (its groups and query blocks)."""
+    g0, g1 = shard.groups
+    i0, i1 = shard.q_blocks
+    rep = shape.q_heads // shape.kv_heads
+    entries = sum(min(i + 1, K) for i in range(i0, i1))
+    rows = i1 - i0
+    pairs = (entries - rows) * 64 * 64 + rows * 64 * 65 / 2
+    return 4.0 * shape.head_dim * rep * (g1 - g0) * pairs * shape.batch
+
+
+# ----------------------------------------------------------------- CPU baseline (oracle port)
+def cpu_sample(shape, K, q, k, v, wq, wk, target_s: float, rows: int | None = None):
+    """Time the CPU restatement of the reference path on a bounded sample.
+
+    Sample: KV group 0 (7 query heads) -- its whole selector (pooling, gate,
+    top-k, packing) plus attention of the last M query blocks (each with K
+    selected blocks); M is calibrated so one sample takes ~target_s seconds.
+    Returned TFLOP/s = attention FLOPs of the M rows / (attention time + the
+    selector time prorated to M/qb of the rows).
+    """
+    import torch
+
+    from oracle import oracle as O
+
+    rep = shape.q_heads // shape.kv_heads
+    qb = shape.query_blocks
+    q0 = q[:, 0:rep].transpose(1, 2).contiguous().cpu().transpose(1, 2)
+    k0 = k[:, 0:1].transpose(1, 2).contiguous().cpu().transpose(1, 2)
+    v0 = v[:, 0:1].transpose(1, 2).contiguous().cpu().transpose(1, 2)
+    wq, wk = wq.cpu(), wk.cpu()
+
+    t0 = time.perf_counter()
+    sel = O.select_blocks(q0, k0, wq, wk, K, 0, 1)["selected"]
+    t_sel = time.perf_counter() - t0
+
+    def attn_rows(m):
+        t = time.perf_counter()
+        O.sparse_attention(q0, k0, v0, sel, out_dtype=torch.float32, q_blocks=(qb - m, qb))
+        return time.perf_counter() - t
+
+    m = rows
+    if m is None:
+        t4 = attn_rows(4)
+        m = int(max(1, min(qb, round(4 * max(target_s, 0.5) / max(t4, 1e-3)))))
+    best = attn_rows(m) + t_sel * m / qb
+    rows_flops = 4.0 * shape.head_dim * rep * m * ((K - 1) * 4096 + 64 * 65 / 2)
+    return {
+        "value": rows_flops / best / 1e12, "unit": "TFLOP/s", "cores": O.num_threads(), "kind": "port",
+        "seconds": best,
+        "sample": (f"oracle C port (OpenMP, {O.num_threads()} threads): KV group 0 selector "
+                   f"({t_sel:.2f} s, prorated {m}/{qb}) + attention of the last {m} query blocks x {rep} heads, "
+                   f"K={K}; fp32 math on bf16 inputs"),
+    }, m
+
+
+# ----------------------------------------------------------------- GPU arm
+def run_b200(args):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from spruce_research_b200 import native
+    from spruce_research_b200.pipeline import SparsePrefillLayer
+    from spruce_research_b200.sharding import ShardedSparsePrefill, plan
+    from spruce_research_b200.synthetic import make_gate_weights, make_layer_inputs
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=180))
+
+    shape, K, entries, flops = workload(args)
+    qb = shape.query_blocks
+    q, k, v = make_layer_inputs(shape, torch.bfloat16, args.seed, device=dev)
+    wq, wk = make_gate_weights(1, shape.head_dim, shape.head_dim, args.seed + 1, device=dev)
+    layer = SparsePrefillLayer(wq[0], wk[0], K, local_window=0, sink_blocks=1)
+    shard = plan(world, rank, shape.kv_heads, qb)
+    runner = ShardedSparsePrefill(shard, layer)
+    g0, g1 = shard.groups
+    rep = shape.q_heads // shape.kv_heads
+    i0, i1 = shard.q_blocks
+    B, T, D = shape.batch, shape.tokens, shape.head_dim
+    local_out = torch.empty((B, T, (g1 - g0) * rep, D), device=dev, dtype=torch.bfloat16)
+    sel_buf = torch.empty((B, g1 - g0, qb, K), device=dev, dtype=torch.int32)
+
+    def step(qs, ks, vs, marks=None):
+        """This rank's selector + attention (+ all-gather); q/k/v are its shard's views."""
+        if marks is not None:
+            marks[0].record()
+        sel = layer.select(qs, ks, out=sel_buf)
+        if marks is not None:
+            marks[1].record()
+        native.sparse_attention(qs, ks, vs, sel, out=local_out, q_blocks=(i0, i1))
+        if marks is not None:
+            marks[2].record()
+        full = local_out
+        if world > 1:
+            full = runner.gather(local_out[:, i0 * 64:i1 * 64], shape.kv_heads, T)
+        if marks is not None:
+            marks[3].record()
+        return full
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    q_shard, k_shard, v_shard = q[:, g0 * rep:g1 * rep], k[:, g0:g1], v[:, g0:g1]
+    for _ in range(args.warmup):
+        step(q_shard, k_shard, v_shard)
+    barrier()
+    marks = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier()
+        start.record()
+        for s in range(args.steps):
+            step(q_shard, k_shard, v_shard, marks[s])
+        stop.record()
+        barrier()
+    elapsed_ms = max_over_ranks(start.elapsed_time(stop))
+    ms = elapsed_ms / args.steps
+    sel_ms = statistics.mean(m[0].elapsed_time(m[1]) for m in marks)
+    attn_ms = statistics.mean(m[1].elapsed_time(m[2]) for m in marks)
+    gather_ms = statistics.mean(m[2].elapsed_time(m[3]) for m in marks)
+    attn_ms_max = max_over_ranks(attn_ms)
+    sel_ms_max = max_over_ranks(sel_ms)
+    gather_ms_max = max_over_ranks(gather_ms)
+
+    # ---- end to end through the public API with pinned host buffers
+    e2e = None
+    if not args.no_e2e:
+        hq = q[:, g0 * rep:g1 * rep].transpose(1, 2).contiguous().cpu().pin_memory()   # [B, T, Hr, D]
+        hk = k[:, g0:g1].transpose(1, 2).contiguous().cpu().pin_memory()
+        hv = v[:, g0:g1].transpose(1, 2).contiguous().cpu().pin_memory()
+        dq, dk, dv = (torch.empty_like(t, device=dev) for t in (hq, hk, hv))
+        hout = torch.empty((B, T, shape.q_heads, D), dtype=torch.bfloat16).pin_memory() if rank == 0 else None
+
+        def e2e_step():
+            dq.copy_(hq, non_blocking=True)
+            dk.copy_(hk, non_blocking=True)
+            dv.copy_(hv, non_blocking=True)
+            out = step(dq.transpose(1, 2), dk.transpose(1, 2), dv.transpose(1, 2))
+            if rank == 0:
+                hout.copy_(out, non_blocking=True)
+
+        for _ in range(max(1, args.warmup)):
+            e2e_step()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record()
+        barrier()
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+        e2e = {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
+               "h2d_bytes_per_step": int(sum(t.numel() * t.element_size() for t in (hq, hk, hv))),
+               "d2h_bytes_per_step": int(hout.numel() * hout.element_size()) if rank == 0 else 0,
+               "path": "pinned host Q/K/V -> SparsePrefillLayer (selector + attention) -> pinned host output"}
+        del dq, dk, dv
+
+    # ---- CPU baseline (rank 0, single GPU only)
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu, _ = cpu_sample(shape, K, q, k, v, wq[0], wk[0], args.cpu_seconds)
+
+    peak, peak_src = measured_peak()
+    r_flops = shard_flops(shape, K, shard)
+    achieved = r_flops / (attn_ms * 1e-3) / 1e12
+    result = {
+        "metric": METRIC,
+        "value": flops / (ms * 1e-3) / 1e12,
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "ms_per_layer": ms,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1) Q/K/V, RoPE base 1e6, planted affinity (3 blocks/query block)",
+        "config": config_dict(args, shape, K, entries, world),
+        "breakdown_ms": {"selector": sel_ms_max, "attention": attn_ms_max, "gather": gather_ms_max},
+        "roofline": {"bound": "tensor", "kernel": "attn_fwd_sm100_kernel<bf16,128,3>",
+                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                     "peak_source": peak_src + ", of measured",
+                     "flops_per_launch": r_flops, "traffic": profiled_traffic(shape.tokens)},
+        "gpu_launches": SparsePrefillLayer.LAUNCHES_PER_CALL * args.steps,
+        "clocks": clocks.summary(),
+    }
+    if e2e is not None:
+        result["e2e"] = e2e
+    if cpu is not None:
+        result["cpu_baseline"] = cpu
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+# ----------------------------------------------------------------- reference arm
+def run_reference(args):
+    """CPU restatement of the reference path (oracle port) on the host cores, rank 0 only."""
+    import torch
+
+    from spruce_research_b200.synthetic import make_gate_weights, make_layer_inputs
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    shape, K, entries, flops = workload(args)
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    q, k, v = make_layer_inputs(shape, torch.bfloat16, args.seed, device=dev)
+    wq, wk = make_gate_weights(1, shape.head_dim, shape.head_dim, args.seed + 1, device=dev)
+    # Size the sample once (about cpu_seconds of CPU work), then time it per step.
+    info, m = cpu_sample(shape, K, q, k, v, wq[0], wk[0], target_s=min(args.cpu_seconds, 8.0))
+    steps = []
+    for s in range(args.warmup + args.steps):
+        r, _ = cpu_sample(shape, K, q, k, v, wq[0], wk[0], 0.0, rows=m)
+        if s >= args.warmup:
+            steps.append(r["value"])
+            info = r
+    value = statistics.median(steps)
+    ms = flops / (value * 1e12) * 1e3
+    result = {
+        "metric": METRIC, "impl": "reference", "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "ms_per_layer": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1) Q/K/V, RoPE base 1e6, planted affinity (3 blocks/query block)",
+        "config": config_dict(args, shape, K, entries, args.gpus),
+        "cpu_baseline": {**info, "value": value},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "ms_per_step extrapolates the sample's rate to the whole layer",
+    }
+    print(json.dumps(result), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -173,6 +173,20 @@ SPRUCE_API int spruce_sparse_attention_fwd(const void *q, const int64_t q_stride
                                 const int64_t out_strides[4], int dtype, int64_t B, int64_t Hq, int64_t Hkv,
                                 int64_t T, int64_t D, int64_t Kw, float scale, uint32_t *status, void *stream);
 
+/*
+ * spruce_sparse_attention_fwd restricted to query blocks [q_block_begin,
+ * q_block_end): only those output rows are written.  Used to split one
+ * layer's query blocks across GPUs; the block ids keep their absolute values.
+ */
+SPRUCE_API int spruce_sparse_attention_fwd_rows(const void *q, const int64_t q_strides[4], const void *k,
+                                                const int64_t k_strides[4], const void *v,
+                                                const int64_t v_strides[4], const int32_t *indices,
+                                                const int64_t idx_strides[4], void *out,
+                                                const int64_t out_strides[4], int dtype, int64_t B, int64_t Hq,
+                                                int64_t Hkv, int64_t T, int64_t D, int64_t Kw, float scale,
+                                                int64_t q_block_begin, int64_t q_block_end, uint32_t *status,
+                                                void *stream);
+
 #ifdef __cplusplus
 }
 #endif

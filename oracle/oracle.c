@@ -331,11 +331,26 @@ int oracle_pack_ids(const int64_t *ids, int64_t R, int64_t qb, int64_t C, int64_
  * q: [B, Hq, T, D] fp32, k/v: [B, Hkv, T, D] fp32, idx: [B, Hkv, qb, Kw]
  * int32; out: [B, T, Hq, D] fp32 (token-major like the reference's return).
  */
+void oracle_sparse_attention_rows(const float *q, const float *k, const float *v,
+                                  const int32_t *idx, int64_t B, int64_t Hq, int64_t Hkv,
+                                  int64_t T, int64_t D, int64_t Kw, int64_t block, float scale,
+                                  int64_t q_begin, int64_t q_end, float *out);
+
 void oracle_sparse_attention(const float *q, const float *k, const float *v,
                              const int32_t *idx, int64_t B, int64_t Hq, int64_t Hkv,
                              int64_t T, int64_t D, int64_t Kw, int64_t block, float scale,
                              float *out) {
     const int64_t qb = (T + block - 1) / block;
+    oracle_sparse_attention_rows(q, k, v, idx, B, Hq, Hkv, T, D, Kw, block, scale, 0, qb, out);
+}
+
+/* Same, restricted to query blocks [q_begin, q_end) (other output rows untouched). */
+void oracle_sparse_attention_rows(const float *q, const float *k, const float *v,
+                                  const int32_t *idx, int64_t B, int64_t Hq, int64_t Hkv,
+                                  int64_t T, int64_t D, int64_t Kw, int64_t block, float scale,
+                                  int64_t q_begin, int64_t q_end, float *out) {
+    const int64_t qb = (T + block - 1) / block;
+    const int64_t nq = q_end - q_begin;
     const int64_t rep = Hq / Hkv;
 #pragma omp parallel
     {
@@ -343,10 +358,11 @@ void oracle_sparse_attention(const float *q, const float *k, const float *v,
         float *s = (float *)malloc(sizeof(float) * (size_t)(Kw * block + 1));
         double *acc = (double *)malloc(sizeof(double) * (size_t)D);
 #pragma omp for schedule(dynamic, 1)
-        for (int64_t unit = 0; unit < B * Hkv * qb; ++unit) {
-            const int64_t b = unit / (Hkv * qb);
-            const int64_t g = (unit / qb) % Hkv;
-            const int64_t i = unit % qb;
+        for (int64_t unit = 0; unit < B * Hkv * nq * rep; ++unit) {
+            const int64_t hh = unit % rep;
+            const int64_t b = unit / (Hkv * nq * rep);
+            const int64_t g = (unit / (nq * rep)) % Hkv;
+            const int64_t i = q_begin + (unit / rep) % nq;
             const int32_t *row = idx + (((size_t)b * Hkv + g) * qb + i) * Kw;
             int64_t nk = 0;
             for (int64_t c = 0; c < Kw; ++c) {
@@ -358,7 +374,7 @@ void oracle_sparse_attention(const float *q, const float *k, const float *v,
             }
             const float *kg = k + ((size_t)b * Hkv + g) * T * D;
             const float *vg = v + ((size_t)b * Hkv + g) * T * D;
-            for (int64_t hh = 0; hh < rep; ++hh) {
+            {
                 const int64_t h = g * rep + hh;
                 for (int64_t t = i * block; t < (i + 1) * block && t < T; ++t) {
                     const float *qr = q + (((size_t)b * Hq + h) * T + t) * D;

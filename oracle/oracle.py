@@ -44,8 +44,11 @@ def build() -> str:
 def lib():
     global _lib
     if _lib is None:
-        if not os.path.exists(_LIB_PATH):
-            build()
+        try:
+            build()  # make is incremental: rebuilds only when oracle.c changed
+        except (OSError, subprocess.CalledProcessError):
+            if not os.path.exists(_LIB_PATH):
+                raise
         L = ctypes.CDLL(_LIB_PATH)
         P, I64, F = ctypes.c_void_p, ctypes.c_int64, ctypes.c_float
         L.oracle_group_avg.argtypes = [P, ctypes.c_int, I64, I64, I64, I64, I64, P]
@@ -57,6 +60,7 @@ def lib():
         L.oracle_pack_ids.argtypes = [P, I64, I64, I64, I64, I64, I64, I64, P]
         L.oracle_pack_ids.restype = ctypes.c_int
         L.oracle_sparse_attention.argtypes = [P, P, P, P, I64, I64, I64, I64, I64, I64, I64, F, P]
+        L.oracle_sparse_attention_rows.argtypes = [P, P, P, P, I64, I64, I64, I64, I64, I64, I64, F, I64, I64, P]
         L.oracle_num_threads.restype = ctypes.c_int
         _lib = L
     return _lib
@@ -179,23 +183,27 @@ def select_blocks(q: torch.Tensor, k: torch.Tensor, wq: torch.Tensor, wk: torch.
 
 
 def sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices: torch.Tensor,
-                     scale: float | None = None, block: int = 64, out_dtype=None) -> torch.Tensor:
+                     scale: float | None = None, block: int = 64, out_dtype=None,
+                     q_blocks: tuple[int, int] | None = None) -> torch.Tensor:
     """q [B, Hq, T, D], k/v [B, Hkv, T, D], indices int32 [B, Hkv, qb, K].
 
     Returns [B, T, Hq, D] in ``out_dtype`` (default: q's dtype), computed in
-    fp32 with double-precision softmax sums.
+    fp32 with double-precision softmax sums.  ``q_blocks=(i0, i1)`` computes
+    only those query blocks (other rows are zero).
     """
     B, Hq, T, D = q.shape
     Hkv = k.shape[1]
     if scale is None:
         scale = D ** -0.5
+    qb = (T + block - 1) // block
+    i0, i1 = (0, qb) if q_blocks is None else q_blocks
     qf = q.detach().float().cpu().contiguous()
     kf = k.detach().float().cpu().contiguous()
     vf = v.detach().float().cpu().contiguous()
     idx = indices.detach().cpu().to(torch.int32).contiguous()
-    out = torch.empty((B, T, Hq, D), dtype=torch.float32)
-    lib().oracle_sparse_attention(_ptr(qf), _ptr(kf), _ptr(vf), _ptr(idx), B, Hq, Hkv, T, D,
-                                  idx.shape[-1], block, float(scale), _ptr(out))
+    out = torch.zeros((B, T, Hq, D), dtype=torch.float32)
+    lib().oracle_sparse_attention_rows(_ptr(qf), _ptr(kf), _ptr(vf), _ptr(idx), B, Hq, Hkv, T, D,
+                                       idx.shape[-1], block, float(scale), i0, i1, _ptr(out))
     return out.to(out_dtype or q.dtype)
 
 

@@ -46,6 +46,8 @@ SIGNATURES = {
     "spruce_validate_selected_blocks": ([_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P], _INT),
     "spruce_sparse_attention_fwd": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _INT, _I64, _I64, _I64, _I64, _I64,
                                      _I64, _F, _P, _P], _INT),
+    "spruce_sparse_attention_fwd_rows": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _INT, _I64, _I64, _I64, _I64,
+                                          _I64, _I64, _F, _I64, _I64, _P, _P], _INT),
 }
 
 _lib = None

@@ -23,7 +23,7 @@ struct F32Params {
   int64_t isb, isg, isq;
   float* out;
   int64_t osb, osh, ost;
-  int Hq, Hkv, T, Kw, qb, rep;
+  int Hq, Hkv, T, Kw, qb, rep, q_begin, nq;
   float scale;
   uint32_t* status;
 };
@@ -39,7 +39,7 @@ __global__ void __launch_bounds__(256) attn_fwd_f32_kernel(const F32Params p) {
   int* ids = reinterpret_cast<int*>(Ps + 64 * 65);
   __shared__ int nsel;
 
-  const int i = p.qb - 1 - blockIdx.x;
+  const int i = p.q_begin + p.nq - 1 - blockIdx.x;
   const int h = blockIdx.y;
   const int b = blockIdx.z;
   const int g = h / p.rep;
@@ -160,12 +160,15 @@ static cudaError_t launch_f32_typed(const AttnArgs& a, cudaStream_t stream) {
   p.Hq = a.Hq; p.Hkv = a.Hkv; p.T = a.T; p.Kw = a.Kw;
   p.qb = (a.T + 63) / 64;
   p.rep = a.Hq / a.Hkv;
+  p.q_begin = a.q_begin;
+  p.nq = a.q_end - a.q_begin;
   p.scale = a.scale;
   p.status = a.status;
   const size_t smem = sizeof(float) * (64 * D + 64 * (D + 4) + 64 * D + 64 * 65) + sizeof(int) * (size_t)a.Kw;
   cudaError_t e = cudaFuncSetAttribute(attn_fwd_f32_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  dim3 grid(p.qb, a.Hq, a.B);
+  if (p.nq <= 0) return cudaSuccess;
+  dim3 grid(p.nq, a.Hq, a.B);
   attn_fwd_f32_kernel<D><<<grid, 256, smem, stream>>>(p);
   return cudaGetLastError();
 }

@@ -17,15 +17,20 @@
 //   warps 4-7  softmax + epilogue of tile 1
 //   warp  8    TMA producer (Q once, then K/V of each selected block, STAGES ring)
 //   warp  9    TMEM allocator + single-thread MMA issuer
+//
 // Per selected block j and tile t:
 //   S_t = Q_t K_j^T      (M=128, N=64, K=D; A, B K-major, 128B swizzle)
-//   softmax_t: S -> P (bf16/fp16, swizzled smem), lazy O rescale (only when
-//              the running max grows by more than 8 in log2 units)
-//   O_t += P_t V_j       (M=128, N=D, K=64; B MN-major)
-// The MMA warp interleaves the tiles: PV_0(j), S_0(j+1), PV_1(j), S_1(j+1),
-// so one tile's softmax overlaps the other tile's tensor-core work.
+//   softmax_t: S_t -> registers (then S_t is released, so S_t(j+1) runs on
+//              the tensor cores while this block's exponentials are computed)
+//              -> P (bf16/fp16) into TMEM buffer P_t[j % 2]; O is rescaled
+//              only when the running max grows by more than 8 in log2 units
+//              (the final O / l is unaffected by the reference max used).
+//   O_t += P_t[j % 2] V_j  (A from TMEM, B = V MN-major in smem, N = D)
+// MMA issue order per block: S_0(j+1), S_1(j+1) as soon as each S buffer is
+// released, then PV_0(j), PV_1(j).  A P buffer is rewritten only after the PV
+// that read it has completed (one completion barrier per P buffer).
 //
-// TMEM columns: O_0 [0, D), O_1 [D, 2D), S_0 [2D, 2D+64), S_1 [2D+64, 2D+128).
+// TMEM columns: O_t at [t*D, (t+1)*D); S_t at 2D + 64t; P_t[b] at 2D + 128 + 64t + 32b.
 #include <algorithm>
 
 #include "common.cuh"
@@ -43,6 +48,7 @@ struct AttnParams {
   void* out;
   int64_t osb, osh, ost;
   int Hq, Hkv, T, Kw, qb, rep, n_pair, n_cta;
+  int q_begin, nq;  // query blocks [q_begin, q_begin + nq) are computed
   float scale_log2;
   uint32_t* status;
 };
@@ -54,18 +60,17 @@ struct AttnLayout {
   static constexpr int KV_PANEL = 64 * 128;          // 64 rows x 128 B
   static constexpr int Q_TILE = NP * Q_PANEL;
   static constexpr int KV_TILE = NP * KV_PANEL;
-  static constexpr int P_TILE = 128 * 128;           // 128 rows x 64 keys x 2 B
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + 2 * Q_TILE;
   static constexpr int OFF_V = OFF_K + STAGES * KV_TILE;
-  static constexpr int OFF_P = OFF_V + STAGES * KV_TILE;
-  static constexpr int OFF_BAR = OFF_P + 2 * P_TILE;
-  // q_full, k_full[S], v_full[S], kv_empty[S], s_full[2], p_full[2], o_done[2], drain
-  static constexpr int NBAR = 1 + 3 * STAGES + 7;
+  static constexpr int OFF_BAR = OFF_V + STAGES * KV_TILE;
+  // q_full, k_full[S], v_full[S], kv_empty[S], s_full[2], s_free[2], p_full[2][2], o_done[2][2], drain
+  static constexpr int NBAR = 1 + 3 * STAGES + 2 + 2 + 4 + 4 + 1;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int OFF_IDS = OFF_MISC + 16;
-  static constexpr int COL_O0 = 0, COL_O1 = D, COL_S0 = 2 * D, COL_S1 = 2 * D + 64;
-  static constexpr uint32_t TMEM_COLS = (2 * D + 128 <= 256) ? 256u : 512u;
+  static constexpr int COL_S = 2 * D;                // S_t at COL_S + 64 t
+  static constexpr int COL_P = 2 * D + 128;          // P_t[b] at COL_P + 64 t + 32 b
+  static constexpr uint32_t TMEM_COLS = (2 * D + 256 <= 256) ? 256u : 512u;
   static size_t smem_bytes(int kw) { return 1024 + OFF_IDS + 4 * (size_t)kw; }
 };
 
@@ -83,6 +88,30 @@ template <> struct Pack2<__half> {
   }
 };
 
+// D[tmem] (+)= A[tmem] * B[smem], kind::f16.  A has M rows = TMEM lanes and K
+// packed two 16-bit values per 32-bit column (8 columns per K = 16 step).
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
 template <typename T, int D, int STAGES>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
@@ -93,7 +122,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int i = p.qb - 1 - static_cast<int>(blockIdx.x) / p.n_cta;  // late (heavy) rows first
+  const int i = p.q_begin + p.nq - 1 - static_cast<int>(blockIdx.x) / p.n_cta;  // late (heavy) rows first
   const int c = static_cast<int>(blockIdx.x) % p.n_cta;
   const int g = blockIdx.y;
   const int b = blockIdx.z;
@@ -105,10 +134,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* k_full = bars + 1;
   uint64_t* v_full = k_full + STAGES;
   uint64_t* kv_empty = v_full + STAGES;
-  uint64_t* s_full = kv_empty + STAGES;
-  uint64_t* p_full = s_full + 2;
-  uint64_t* o_done = p_full + 2;
-  uint64_t* drain = o_done + 2;
+  uint64_t* s_full = kv_empty + STAGES;  // [tile]
+  uint64_t* s_free = s_full + 2;         // [tile]
+  uint64_t* p_full = s_free + 2;         // [tile * 2 + P buffer]
+  uint64_t* o_done = p_full + 4;         // [tile * 2 + P buffer]: PV that read that buffer is done
+  uint64_t* drain = o_done + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
   int* nsel_slot = reinterpret_cast<int*>(smem + L::OFF_MISC + 8);
@@ -137,8 +167,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       for (int t = 0; t < 2; ++t) {
         mbar_init(&s_full[t], 1);
-        mbar_init(&p_full[t], 128);
-        mbar_init(&o_done[t], 1);
+        mbar_init(&s_free[t], 128);
+      }
+      for (int x = 0; x < 4; ++x) {
+        mbar_init(&p_full[x], 128);
+        mbar_init(&o_done[x], 1);
       }
       mbar_init(drain, 1);
       fence_barrier_init();
@@ -159,25 +192,37 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   if (warp == kProducerWarp) {
     // ------------------------------------------------------------ TMA producer
-    if (lane == 0 && n > 0) {
+    // The whole warp runs the loop (waits are warp-uniform); one elected lane issues.
+    if (n > 0) {
+      const bool leader = elect_one();
       uint8_t* qs = smem + L::OFF_Q;
-      mbar_arrive_expect_tx(q_full, n_tiles * L::Q_TILE);
-      for (int t = 0; t < n_tiles; ++t) {
-        const int h0 = g * p.rep + 2 * (pair0 + t);
-        for (int pp = 0; pp < L::NP; ++pp)
-          tma_load_4d(qs + t * L::Q_TILE + pp * L::Q_PANEL, &tmq, q_full, pp * 64, h0, i * 64, b);
+      if (leader) {
+        mbar_arrive_expect_tx(q_full, n_tiles * L::Q_TILE);
+        for (int t = 0; t < n_tiles; ++t) {
+          const int h0 = g * p.rep + 2 * (pair0 + t);
+          for (int pp = 0; pp < L::NP; ++pp)
+            tma_load_4d(qs + t * L::Q_TILE + pp * L::Q_PANEL, &tmq, q_full, pp * 64, h0, i * 64, b);
+        }
       }
+      __syncwarp();
       int issued = 0;
       for (int j = 0; j < n; ++j) {
         const int st = j % STAGES;
-        if (j >= STAGES && !mbar_wait(&kv_empty[st], ((j / STAGES) - 1) & 1, p.status, abort_flag)) break;
-        const int tok = ids[j] * 64;
-        uint8_t* ks = smem + L::OFF_K + st * L::KV_TILE;
-        uint8_t* vs = smem + L::OFF_V + st * L::KV_TILE;
-        mbar_arrive_expect_tx(&k_full[st], L::KV_TILE);
-        for (int pp = 0; pp < L::NP; ++pp) tma_load_4d(ks + pp * L::KV_PANEL, &tmk, &k_full[st], pp * 64, g, tok, b);
-        mbar_arrive_expect_tx(&v_full[st], L::KV_TILE);
-        for (int pp = 0; pp < L::NP; ++pp) tma_load_4d(vs + pp * L::KV_PANEL, &tmv, &v_full[st], pp * 64, g, tok, b);
+        if (j >= STAGES &&
+            !__all_sync(0xffffffffu, mbar_wait(&kv_empty[st], ((j / STAGES) - 1) & 1, p.status, abort_flag)))
+          break;
+        if (leader) {
+          const int tok = ids[j] * 64;
+          uint8_t* ks = smem + L::OFF_K + st * L::KV_TILE;
+          uint8_t* vs = smem + L::OFF_V + st * L::KV_TILE;
+          mbar_arrive_expect_tx(&k_full[st], L::KV_TILE);
+          for (int pp = 0; pp < L::NP; ++pp)
+            tma_load_4d(ks + pp * L::KV_PANEL, &tmk, &k_full[st], pp * 64, g, tok, b);
+          mbar_arrive_expect_tx(&v_full[st], L::KV_TILE);
+          for (int pp = 0; pp < L::NP; ++pp)
+            tma_load_4d(vs + pp * L::KV_PANEL, &tmv, &v_full[st], pp * 64, g, tok, b);
+        }
+        __syncwarp();
         issued = j + 1;
       }
       // No copy may be in flight when the CTA exits: wait for the last loads.
@@ -190,67 +235,92 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     __syncwarp();
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0 && n > 0) {
+    // The whole warp runs the schedule; one elected lane issues each tcgen05 op.
+    if (n > 0) {
+      const bool leader = elect_one();
       constexpr uint32_t fmt = UmmaFormat<T>::value;
       constexpr uint32_t idesc_qk = idesc_f16(fmt, 0, 0, 64, 128);
       constexpr uint32_t idesc_pv = idesc_f16(fmt, 0, 1, D, 128);
-      const uint32_t q_base = smem_u32(smem + L::OFF_Q);
-      const uint32_t k_base = smem_u32(smem + L::OFF_K);
-      const uint32_t v_base = smem_u32(smem + L::OFF_V);
-      const uint32_t p_base = smem_u32(smem + L::OFF_P);
-      const uint32_t s_col[2] = {tmem + L::COL_S0, tmem + L::COL_S1};
-      const uint32_t o_col[2] = {tmem + L::COL_O0, tmem + L::COL_O1};
+      // Descriptors are built once; per MMA only the start address (low 14 bits,
+      // 16-byte units, no carry: shared memory is < 256 KB) is advanced.
+      const uint64_t dq0 = smem_desc(smem_u32(smem + L::OFF_Q), 16, 1024);
+      const uint64_t dk0 = smem_desc(smem_u32(smem + L::OFF_K), 16, 1024);
+      const uint64_t dv0 = smem_desc(smem_u32(smem + L::OFF_V), L::KV_PANEL, 1024);
 
       auto issue_qk = [&](int t, int st) {
         // S_t = Q_t . K^T over D in steps of 16 (32 bytes inside a 128-byte swizzle row).
+        const uint32_t d = tmem + L::COL_S + 64 * t;
+        const uint64_t qa = dq0 + (uint64_t)((t * L::Q_TILE) >> 4);
+        const uint64_t kb = dk0 + (uint64_t)((st * L::KV_TILE) >> 4);
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {
-          const uint32_t off = (ks & 3) * 32;
-          const uint64_t a = smem_desc(q_base + t * L::Q_TILE + (ks >> 2) * L::Q_PANEL + off, 16, 1024);
-          const uint64_t bb = smem_desc(k_base + st * L::KV_TILE + (ks >> 2) * L::KV_PANEL + off, 16, 1024);
-          umma_f16_ss(s_col[t], a, bb, idesc_qk, ks > 0 ? 1u : 0u);
+          const uint32_t offq = ((ks >> 2) * L::Q_PANEL + (ks & 3) * 32) >> 4;
+          const uint32_t offk = ((ks >> 2) * L::KV_PANEL + (ks & 3) * 32) >> 4;
+          if (leader) umma_f16_ss(d, qa + offq, kb + offk, idesc_qk, ks > 0 ? 1u : 0u);
+          __syncwarp();
         }
       };
-      auto issue_pv = [&](int t, int st, bool accumulate) {
-        // O_t += P_t . V over the 64 keys in steps of 16 keys (2048 bytes of V).
+      auto issue_pv = [&](int t, int st, int buf, bool accumulate) {
+        // O_t += P_t[buf] . V over 64 keys in steps of 16 keys (8 TMEM columns of P, 2048 bytes of V).
+        const uint32_t a = tmem + L::COL_P + 64 * t + 32 * buf;
+        const uint64_t vb = dv0 + (uint64_t)((st * L::KV_TILE) >> 4);
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks) {
-          const uint64_t a = smem_desc(p_base + t * L::P_TILE + ks * 32, 16, 1024);
-          const uint64_t bb = smem_desc(v_base + st * L::KV_TILE + ks * 2048, L::KV_PANEL, 1024);
-          umma_f16_ss(o_col[t], a, bb, idesc_pv, (accumulate || ks > 0) ? 1u : 0u);
+          if (leader)
+            umma_f16_ts(tmem + t * D, a + ks * 8, vb + (uint64_t)((ks * 2048) >> 4), idesc_pv,
+                        (accumulate || ks > 0) ? 1u : 0u);
+          __syncwarp();
         }
       };
+      auto commit = [&](uint64_t* bar) {
+        if (leader) umma_commit(bar);
+        __syncwarp();
+      };
+      auto wait = [&](uint64_t* bar, uint32_t parity) {
+        return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.status, abort_flag));
+      };
 
-      bool ok = mbar_wait(q_full, 0, p.status, abort_flag) && mbar_wait(&k_full[0], 0, p.status, abort_flag);
+      bool ok = wait(q_full, 0) && wait(&k_full[0], 0);
       if (ok) {
         tc_fence_after();
         for (int t = 0; t < n_tiles; ++t) {
           issue_qk(t, 0);
-          umma_commit(&s_full[t]);
+          commit(&s_full[t]);
         }
       }
       for (int j = 0; ok && j < n; ++j) {
         const int st = j % STAGES;
-        const int st1 = (j + 1) % STAGES;
-        if (!mbar_wait(&v_full[st], (j / STAGES) & 1, p.status, abort_flag)) break;
-        if (j + 1 < n && !mbar_wait(&k_full[st1], ((j + 1) / STAGES) & 1, p.status, abort_flag)) break;
+        const int buf = j & 1;
+        if (j + 1 < n) {
+          // S(j+1) as soon as the softmax has taken S(j) into registers.
+          const int st1 = (j + 1) % STAGES;
+          if (!wait(&k_full[st1], ((j + 1) / STAGES) & 1)) break;
+          for (int t = 0; t < n_tiles; ++t) {
+            if (!wait(&s_free[t], j & 1)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_qk(t, st1);
+            commit(&s_full[t]);
+          }
+          if (!ok) break;
+        }
+        if (!wait(&v_full[st], (j / STAGES) & 1)) break;
         for (int t = 0; t < n_tiles; ++t) {
-          if (!mbar_wait(&p_full[t], j & 1, p.status, abort_flag)) {
+          if (!wait(&p_full[2 * t + buf], (j >> 1) & 1)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          issue_pv(t, st, j > 0);
-          umma_commit(&o_done[t]);
-          if (t == n_tiles - 1) umma_commit(&kv_empty[st]);
-          if (j + 1 < n) {
-            issue_qk(t, st1);
-            umma_commit(&s_full[t]);
-          }
+          issue_pv(t, st, buf, j > 0);
+          commit(&o_done[2 * t + buf]);
         }
+        if (!ok) break;
+        commit(&kv_empty[st]);
       }
       // No MMA may be in flight when TMEM is released.
-      umma_commit(drain);
+      commit(drain);
       mbar_wait(drain, 0, p.status, nullptr);
     }
     __syncwarp();
@@ -260,83 +330,93 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int row = (warp & 3) * 32 + lane;  // TMEM lane == tile row
     const int tok = row >> 1;                // token within the query block
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t tS = tmem + lane_off + (t ? L::COL_S1 : L::COL_S0);
-    const uint32_t tO = tmem + lane_off + (t ? L::COL_O1 : L::COL_O0);
-    uint8_t* Ps = smem + L::OFF_P + t * L::P_TILE;
+    const uint32_t tO = tmem + lane_off + t * D;
     if (t < n_tiles) {
-      float m_used = -INFINITY;
+      const float sl2 = p.scale_log2;
+      float m_used = -INFINITY;  // reference max (log2 units) the exponentials use
       float l = 0.0f;
       bool ok = true;
+      const uint32_t tS = tmem + lane_off + L::COL_S + 64 * t;
       for (int j = 0; j < n; ++j) {
+        const int buf = j & 1;
         ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], j & 1, p.status, abort_flag));
         if (!ok) break;
         tc_fence_after();
-        float sa[32], sb[32];
-        tmem_ld32(tS, sa);
-        tmem_ld32(tS + 32, sb);
-        tmem_wait_ld();
         float s[64];
+        {
+          float sa[32], sb[32];
+          tmem_ld32(tS, sa);
+          tmem_ld32(tS + 32, sb);
+          tmem_wait_ld();
 #pragma unroll
-        for (int cc = 0; cc < 32; ++cc) {
-          s[cc] = sa[cc];
-          s[cc + 32] = sb[cc];
+          for (int cc = 0; cc < 32; ++cc) {
+            s[cc] = sa[cc];
+            s[cc + 32] = sb[cc];
+          }
         }
-        const bool diag = ids[j] == i;
-        float mx = -INFINITY;
+        tc_fence_before();
+        mbar_arrive(&s_free[t]);  // S_t may now be overwritten by S_t(j+1)
+        if (ids[j] == i) {        // diagonal block: keys after the row's token are masked
 #pragma unroll
-        for (int cc = 0; cc < 64; ++cc) {
-          float x = s[cc] * p.scale_log2;
-          if (diag && cc > tok) x = -INFINITY;
-          s[cc] = x;
-          mx = fmaxf(mx, x);
+          for (int cc = 0; cc < 64; ++cc)
+            if (cc > tok) s[cc] = -INFINITY;
         }
-        const float m_new = fmaxf(m_used, mx);
+        // Row max as a tree (exact in any order).
+        float mx8[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          mx8[u] = fmaxf(fmaxf(fmaxf(s[u], s[u + 8]), fmaxf(s[u + 16], s[u + 24])),
+                         fmaxf(fmaxf(s[u + 32], s[u + 40]), fmaxf(s[u + 48], s[u + 56])));
+        }
+        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        const float m_new = fmaxf(m_used, mx * sl2);
         const bool rescale = (j == 0) || (m_new > m_used + 8.0f);
-        if (j > 0) {
-          // PV(j-1) must be complete before P is overwritten or O is rescaled.
-          ok = __all_sync(0xffffffffu, mbar_wait(&o_done[t], (j - 1) & 1, p.status, abort_flag));
+        if (j > 0 && __any_sync(0xffffffffu, rescale)) {
+          // PV(j-1) must be complete before O is rescaled.
+          ok = __all_sync(0xffffffffu, mbar_wait(&o_done[2 * t + (buf ^ 1)], ((j - 1) >> 1) & 1, p.status,
+                                                 abort_flag));
           if (!ok) break;
           tc_fence_after();
-          if (__any_sync(0xffffffffu, rescale)) {
-            const float alpha = rescale ? fast_exp2(m_used - m_new) : 1.0f;
+          const float alpha = rescale ? fast_exp2(m_used - m_new) : 1.0f;
 #pragma unroll 1
-            for (int cc = 0; cc < D / 32; ++cc) {
-              float o[32];
-              tmem_ld32(tO + cc * 32, o);
-              tmem_wait_ld();
+          for (int cc = 0; cc < D / 32; ++cc) {
+            float o[32];
+            tmem_ld32(tO + cc * 32, o);
+            tmem_wait_ld();
 #pragma unroll
-              for (int e = 0; e < 32; ++e) o[e] *= alpha;
-              tmem_st32(tO + cc * 32, o);
-            }
-            tmem_wait_st();
-            l *= alpha;
+            for (int e = 0; e < 32; ++e) o[e] *= alpha;
+            tmem_st32(tO + cc * 32, o);
           }
+          tmem_wait_st();
+          l *= alpha;
         }
         if (rescale) m_used = m_new;
-        const float mref = (m_used == -INFINITY) ? 0.0f : m_used;
-        float sum = 0.0f;
-        uint8_t* prow = Ps + row * 128;
+        const float neg_ref = (m_used == -INFINITY) ? 0.0f : -m_used;
+        uint32_t pk[32];
+        float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          float e[8];
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            e[k] = fast_exp2(s[ch * 8 + k] - mref);
-            sum += e[k];
-          }
-          uint4 v;
-          v.x = Pack2<T>::pack(e[0], e[1]);
-          v.y = Pack2<T>::pack(e[2], e[3]);
-          v.z = Pack2<T>::pack(e[4], e[5]);
-          v.w = Pack2<T>::pack(e[6], e[7]);
-          *reinterpret_cast<uint4*>(prow + ((ch ^ (row & 7)) << 4)) = v;
+        for (int cc = 0; cc < 32; ++cc) {
+          const float e0 = fast_exp2(fmaf(s[2 * cc], sl2, neg_ref));
+          const float e1 = fast_exp2(fmaf(s[2 * cc + 1], sl2, neg_ref));
+          part[cc & 3] += e0 + e1;
+          pk[cc] = Pack2<T>::pack(e0, e1);
         }
-        l += sum;
-        fence_proxy_async_smem();
+        l += (part[0] + part[1]) + (part[2] + part[3]);
+        // P_t[buf] was last read by PV(j-2): it must be complete before it is overwritten.
+        if (j >= 2) {
+          ok = __all_sync(0xffffffffu, mbar_wait(&o_done[2 * t + buf], ((j - 2) >> 1) & 1, p.status, abort_flag));
+          if (!ok) break;
+          tc_fence_after();
+        }
+        tmem_st32u(tmem + lane_off + L::COL_P + 64 * t + 32 * buf, pk);
+        tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(&p_full[t]);
+        mbar_arrive(&p_full[2 * t + buf]);
       }
-      if (ok && n > 0) ok = __all_sync(0xffffffffu, mbar_wait(&o_done[t], (n - 1) & 1, p.status, abort_flag));
+      if (ok && n > 0)  // PV(n-1) complete (and with it every earlier PV into O_t)
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait(&o_done[2 * t + ((n - 1) & 1)], ((n - 1) >> 1) & 1, p.status, abort_flag));
       tc_fence_after();
       // Epilogue: O / l -> T, row (token, head) of the token-major output.
       const int hh = 2 * (pair0 + t) + (row & 1);
@@ -431,6 +511,8 @@ static cudaError_t launch_typed(const AttnArgs& a, CUtensorMapDataType dt, cudaS
   p.T = a.T;
   p.Kw = a.Kw;
   p.qb = (a.T + 63) / 64;
+  p.q_begin = a.q_begin;
+  p.nq = a.q_end - a.q_begin;
   p.rep = a.Hq / a.Hkv;
   p.n_pair = (p.rep + 1) / 2;
   p.n_cta = (p.n_pair + 1) / 2;
@@ -440,7 +522,8 @@ static cudaError_t launch_typed(const AttnArgs& a, CUtensorMapDataType dt, cudaS
   auto kern = attn_fwd_sm100_kernel<T, D, STAGES>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  dim3 grid(p.qb * p.n_cta, a.Hkv, a.B);
+  if (p.nq <= 0) return cudaSuccess;
+  dim3 grid(p.nq * p.n_cta, a.Hkv, a.B);
   kern<<<grid, kAttnThreads, smem, stream>>>(tmq, tmk, tmv, p);
   return cudaGetLastError();
 }
@@ -448,17 +531,17 @@ static cudaError_t launch_typed(const AttnArgs& a, CUtensorMapDataType dt, cudaS
 constexpr size_t kMaxSmem = 227 * 1024;
 
 int attn_sm100_max_kw(int D) {
-  const size_t base = D == 128 ? AttnLayout<128, 3>::smem_bytes(0) : AttnLayout<64, 4>::smem_bytes(0);
+  const size_t base = D == 128 ? AttnLayout<128, 4>::smem_bytes(0) : AttnLayout<64, 4>::smem_bytes(0);
   return static_cast<int>((kMaxSmem - base) / 4);
 }
 
 cudaError_t launch_attn_sm100(const AttnArgs& a, int dtype, cudaStream_t stream) {
   if (a.Kw > attn_sm100_max_kw(a.D)) return cudaErrorInvalidValue;
   if (dtype == SPRUCE_DTYPE_BF16) {
-    if (a.D == 128) return launch_typed<__nv_bfloat16, 128, 3>(a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, stream);
+    if (a.D == 128) return launch_typed<__nv_bfloat16, 128, 4>(a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, stream);
     if (a.D == 64) return launch_typed<__nv_bfloat16, 64, 4>(a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, stream);
   } else if (dtype == SPRUCE_DTYPE_F16) {
-    if (a.D == 128) return launch_typed<__half, 128, 3>(a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, stream);
+    if (a.D == 128) return launch_typed<__half, 128, 4>(a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, stream);
     if (a.D == 64) return launch_typed<__half, 64, 4>(a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, stream);
   }
   return cudaErrorInvalidValue;

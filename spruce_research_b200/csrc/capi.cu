@@ -217,22 +217,28 @@ int spruce_validate_selected_blocks(const int32_t* sel, int64_t B, int64_t L, in
                      "validate launch");
 }
 
-int spruce_sparse_attention_fwd(const void* q, const int64_t q_strides[4], const void* k, const int64_t k_strides[4],
-                                const void* v, const int64_t v_strides[4], const int32_t* indices,
-                                const int64_t idx_strides[4], void* out, const int64_t out_strides[4], int dtype,
-                                int64_t B, int64_t Hq, int64_t Hkv, int64_t T, int64_t D, int64_t Kw, float scale,
-                                uint32_t* status, void* stream) {
+int spruce_sparse_attention_fwd_rows(const void* q, const int64_t q_strides[4], const void* k,
+                                     const int64_t k_strides[4], const void* v, const int64_t v_strides[4],
+                                     const int32_t* indices, const int64_t idx_strides[4], void* out,
+                                     const int64_t out_strides[4], int dtype, int64_t B, int64_t Hq, int64_t Hkv,
+                                     int64_t T, int64_t D, int64_t Kw, float scale, int64_t q_block_begin,
+                                     int64_t q_block_end, uint32_t* status, void* stream) {
   if (!valid_dtype(dtype)) return fail(SPRUCE_ERR_INVALID, "unsupported dtype code %d", dtype);
   if (D != 64 && D != 128) return fail(SPRUCE_ERR_INVALID, "kernel supports head_dim 64 or 128, got %lld", (long long)D);
   if (B < 0 || Hq < 1 || Hkv < 1 || T < 0 || Kw < 0) return fail(SPRUCE_ERR_INVALID, "bad attention shape");
   if (Hq % Hkv) return fail(SPRUCE_ERR_INVALID, "query heads must be divisible by KV heads");
   if (q_strides[3] != 1 || k_strides[3] != 1 || v_strides[3] != 1 || idx_strides[3] != 1 || out_strides[3] != 1)
     return fail(SPRUCE_ERR_INVALID, "q, k, v, and indices must have a contiguous final dimension");
-  if (B == 0 || T == 0) return SPRUCE_OK;
-  if (T > (int64_t)1 << 30 || Hq > 65535 || B > 65535)
+  const int64_t qb = (T + SPRUCE_BLOCK - 1) / SPRUCE_BLOCK;
+  if (q_block_begin < 0 || q_block_end > qb || q_block_begin > q_block_end)
+    return fail(SPRUCE_ERR_INVALID, "query-block range [%lld, %lld) outside [0, %lld)", (long long)q_block_begin,
+                (long long)q_block_end, (long long)qb);
+  if (B == 0 || T == 0 || q_block_begin == q_block_end) return SPRUCE_OK;
+  if (T > (int64_t)1 << 30 || Hkv > 65535 || B > 65535 || qb * 2 > (int64_t)1 << 30)
     return fail(SPRUCE_ERR_UNSUPPORTED, "shape too large for the launch grid");
   spruce::AttnArgs a{q, k, v, q_strides, k_strides, v_strides, indices, idx_strides, out, out_strides,
-                     (int)B, (int)Hq, (int)Hkv, (int)T, (int)D, (int)Kw, scale, status};
+                     (int)B, (int)Hq, (int)Hkv, (int)T, (int)D, (int)Kw, scale, status,
+                     (int)q_block_begin, (int)q_block_end};
   if (dtype == SPRUCE_DTYPE_F32) {
     if (Kw > 8192) return fail(SPRUCE_ERR_UNSUPPORTED, "row width %lld too large", (long long)Kw);
     return cuda_status(spruce::launch_attn_f32(a, as_stream(stream)), "fp32 attention launch");
@@ -249,6 +255,17 @@ int spruce_sparse_attention_fwd(const void* q, const int64_t q_strides[4], const
   if (Kw > spruce::attn_sm100_max_kw((int)D))
     return fail(SPRUCE_ERR_UNSUPPORTED, "row width %lld exceeds %d", (long long)Kw, spruce::attn_sm100_max_kw((int)D));
   return cuda_status(spruce::launch_attn_sm100(a, dtype, as_stream(stream)), "tcgen05 attention launch");
+}
+
+int spruce_sparse_attention_fwd(const void* q, const int64_t q_strides[4], const void* k, const int64_t k_strides[4],
+                                const void* v, const int64_t v_strides[4], const int32_t* indices,
+                                const int64_t idx_strides[4], void* out, const int64_t out_strides[4], int dtype,
+                                int64_t B, int64_t Hq, int64_t Hkv, int64_t T, int64_t D, int64_t Kw, float scale,
+                                uint32_t* status, void* stream) {
+  const int64_t qb = (T + SPRUCE_BLOCK - 1) / SPRUCE_BLOCK;
+  return spruce_sparse_attention_fwd_rows(q, q_strides, k, k_strides, v, v_strides, indices, idx_strides, out,
+                                          out_strides, dtype, B, Hq, Hkv, T, D, Kw, scale, 0, qb < 0 ? 0 : qb,
+                                          status, stream);
 }
 
 }  // extern "C"

@@ -46,6 +46,7 @@ struct AttnArgs {
   int B, Hq, Hkv, T, D, Kw;
   float scale;
   uint32_t* status;
+  int q_begin, q_end;  // query-block range to compute
 };
 
 // tcgen05 path (bf16 / fp16).  Returns cudaErrorInvalidValue for shapes it

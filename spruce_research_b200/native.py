@@ -193,11 +193,12 @@ def validate_first_violation(sel: torch.Tensor, local_window: int) -> tuple[int,
 
 def sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices: torch.Tensor,
                      scale: float | None = None, out: torch.Tensor | None = None,
-                     status: torch.Tensor | None = None) -> torch.Tensor:
+                     status: torch.Tensor | None = None, q_blocks: tuple[int, int] | None = None) -> torch.Tensor:
     """Block-sparse causal GQA attention -> token-major [B, T, Hq, D].
 
     q [B, Hq, T, D], k/v [B, Hkv, T, D] (strided views are fine),
-    indices int32 [B, Hkv, ceil(T/64), K].
+    indices int32 [B, Hkv, ceil(T/64), K].  With ``q_blocks=(i0, i1)`` only
+    query blocks i0..i1-1 are computed (their rows of ``out``).
     """
     _lib.require_cuda(q, k, v, indices)
     B, Hq, T, D = q.shape
@@ -208,14 +209,19 @@ def sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices:
         raise ValueError("q, k and v must share a dtype")
     if indices.dtype != torch.int32:
         raise ValueError("indices must be int32 [B,Hkv,ceil(T/64),K]")
+    qb = (T + BLOCK - 1) // BLOCK
+    if tuple(indices.shape[:3]) != (B, Hkv, qb):
+        raise ValueError("indices must be int32 [B,Hkv,ceil(T/64),K]")
     if out is None:
         out = torch.empty((B, T, Hq, D), device=q.device, dtype=q.dtype)
     ostr = _lib.int64s(out.stride(0), out.stride(2), out.stride(1), out.stride(3))
+    i0, i1 = (0, qb) if q_blocks is None else q_blocks
     L = _lib.load()
-    _lib.check(L.spruce_sparse_attention_fwd(
+    _lib.check(L.spruce_sparse_attention_fwd_rows(
         q.data_ptr(), _lib.strides(q), k.data_ptr(), _lib.strides(k), v.data_ptr(), _lib.strides(v),
         indices.data_ptr(), _lib.strides(indices), out.data_ptr(), ostr, _dt(q), B, Hq, Hkv, T, D,
-        indices.shape[-1], float(scale), status.data_ptr() if status is not None else None, _lib.stream_of(q)))
+        indices.shape[-1], float(scale), i0, i1, status.data_ptr() if status is not None else None,
+        _lib.stream_of(q)))
     return out
 
 
