@@ -12,11 +12,15 @@
 // 7 heads of a Qwen2.5-7B group take 4 tiles (the last half-filled) in two
 // CTAs, and every K/V block a CTA gathers is reused by 2 tiles = 4 heads.
 //
-// Warp roles (320 threads):
+// Warp roles (352 threads):
 //   warps 0-3  softmax + epilogue of tile 0 (TMEM lanes 0-127)
 //   warps 4-7  softmax + epilogue of tile 1
 //   warp  8    TMA producer (Q once, then K/V of each selected block, STAGES ring)
-//   warp  9    TMEM allocator + single-thread MMA issuer
+//   warp  9    TMEM allocator + QK^T issuer
+//   warp 10    PV issuer
+// Two issuing warps: a warp's barrier wait stalls until its own queued MMAs
+// have been handed to the tensor core, so with one issuer every wait left the
+// tensor core idle; with two, one warp's MMAs run while the other waits.
 //
 // Per selected block j and tile t:
 //   S_t = Q_t K_j^T      (M=128, N=64, K=D; A, B K-major, 128B swizzle)
@@ -38,9 +42,10 @@
 
 namespace spruce {
 
-constexpr int kAttnThreads = 320;
+constexpr int kAttnThreads = 352;
 constexpr int kProducerWarp = 8;
-constexpr int kMmaWarp = 9;
+constexpr int kMmaWarp = 9;   // QK^T issuer, owns the TMEM allocation
+constexpr int kPvWarp = 10;   // PV issuer
 
 struct AttnParams {
   const int32_t* idx;
@@ -64,8 +69,8 @@ struct AttnLayout {
   static constexpr int OFF_K = OFF_Q + 2 * Q_TILE;
   static constexpr int OFF_V = OFF_K + STAGES * KV_TILE;
   static constexpr int OFF_BAR = OFF_V + STAGES * KV_TILE;
-  // q_full, k_full[S], v_full[S], kv_empty[S], s_full[2], s_free[2], p_full[2][2], o_done[2][2], drain
-  static constexpr int NBAR = 1 + 3 * STAGES + 2 + 2 + 4 + 4 + 1;
+  // q_full, k_full[S], v_full[S], kv_empty[S], s_full[2], s_free[2], p_full[2][2], o_done[2][2], drain[2]
+  static constexpr int NBAR = 1 + 3 * STAGES + 2 + 2 + 4 + 4 + 2;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int OFF_IDS = OFF_MISC + 16;
   static constexpr int COL_S = 2 * D;                // S_t at COL_S + 64 t
@@ -138,7 +143,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* s_free = s_full + 2;         // [tile]
   uint64_t* p_full = s_free + 2;         // [tile * 2 + P buffer]
   uint64_t* o_done = p_full + 4;         // [tile * 2 + P buffer]: PV that read that buffer is done
-  uint64_t* drain = o_done + 4;
+  uint64_t* drain = o_done + 4;          // [issuer warp]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
   int* nsel_slot = reinterpret_cast<int*>(smem + L::OFF_MISC + 8);
@@ -173,7 +178,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         mbar_init(&p_full[x], 128);
         mbar_init(&o_done[x], 1);
       }
-      mbar_init(drain, 1);
+      mbar_init(&drain[0], 1);
+      mbar_init(&drain[1], 1);
       fence_barrier_init();
       prefetch_tmap(&tmq);
       prefetch_tmap(&tmk);
@@ -233,9 +239,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
     }
     __syncwarp();
-  } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------ MMA issuer
-    // The whole warp runs the schedule; one elected lane issues each tcgen05 op.
+  } else if (warp == kMmaWarp || warp == kPvWarp) {
+    // ------------------------------------------------------------ MMA issuers
+    // Each issuing warp runs its schedule converged; one elected lane issues.
     if (n > 0) {
       const bool leader = elect_one();
       constexpr uint32_t fmt = UmmaFormat<T>::value;
@@ -246,32 +252,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const uint64_t dq0 = smem_desc(smem_u32(smem + L::OFF_Q), 16, 1024);
       const uint64_t dk0 = smem_desc(smem_u32(smem + L::OFF_K), 16, 1024);
       const uint64_t dv0 = smem_desc(smem_u32(smem + L::OFF_V), L::KV_PANEL, 1024);
-
-      auto issue_qk = [&](int t, int st) {
-        // S_t = Q_t . K^T over D in steps of 16 (32 bytes inside a 128-byte swizzle row).
-        const uint32_t d = tmem + L::COL_S + 64 * t;
-        const uint64_t qa = dq0 + (uint64_t)((t * L::Q_TILE) >> 4);
-        const uint64_t kb = dk0 + (uint64_t)((st * L::KV_TILE) >> 4);
-#pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks) {
-          const uint32_t offq = ((ks >> 2) * L::Q_PANEL + (ks & 3) * 32) >> 4;
-          const uint32_t offk = ((ks >> 2) * L::KV_PANEL + (ks & 3) * 32) >> 4;
-          if (leader) umma_f16_ss(d, qa + offq, kb + offk, idesc_qk, ks > 0 ? 1u : 0u);
-          __syncwarp();
-        }
-      };
-      auto issue_pv = [&](int t, int st, int buf, bool accumulate) {
-        // O_t += P_t[buf] . V over 64 keys in steps of 16 keys (8 TMEM columns of P, 2048 bytes of V).
-        const uint32_t a = tmem + L::COL_P + 64 * t + 32 * buf;
-        const uint64_t vb = dv0 + (uint64_t)((st * L::KV_TILE) >> 4);
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {
-          if (leader)
-            umma_f16_ts(tmem + t * D, a + ks * 8, vb + (uint64_t)((ks * 2048) >> 4), idesc_pv,
-                        (accumulate || ks > 0) ? 1u : 0u);
-          __syncwarp();
-        }
-      };
       auto commit = [&](uint64_t* bar) {
         if (leader) umma_commit(bar);
         __syncwarp();
@@ -279,49 +259,71 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       auto wait = [&](uint64_t* bar, uint32_t parity) {
         return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.status, abort_flag));
       };
-
-      bool ok = wait(q_full, 0) && wait(&k_full[0], 0);
-      if (ok) {
-        tc_fence_after();
-        for (int t = 0; t < n_tiles; ++t) {
-          issue_qk(t, 0);
-          commit(&s_full[t]);
-        }
-      }
-      for (int j = 0; ok && j < n; ++j) {
-        const int st = j % STAGES;
-        const int buf = j & 1;
-        if (j + 1 < n) {
-          // S(j+1) as soon as the softmax has taken S(j) into registers.
-          const int st1 = (j + 1) % STAGES;
-          if (!wait(&k_full[st1], ((j + 1) / STAGES) & 1)) break;
+      bool ok = true;
+      if (warp == kMmaWarp) {
+        auto issue_qk = [&](int t, int st) {
+          // S_t = Q_t . K^T over D in steps of 16 (32 bytes inside a 128-byte swizzle row).
+          const uint32_t d = tmem + L::COL_S + 64 * t;
+          const uint64_t qa = dq0 + (uint64_t)((t * L::Q_TILE) >> 4);
+          const uint64_t kb = dk0 + (uint64_t)((st * L::KV_TILE) >> 4);
+#pragma unroll
+          for (int ks = 0; ks < D / 16; ++ks) {
+            const uint32_t offq = ((ks >> 2) * L::Q_PANEL + (ks & 3) * 32) >> 4;
+            const uint32_t offk = ((ks >> 2) * L::KV_PANEL + (ks & 3) * 32) >> 4;
+            if (leader) umma_f16_ss(d, qa + offq, kb + offk, idesc_qk, ks > 0 ? 1u : 0u);
+            __syncwarp();
+          }
+        };
+        ok = wait(q_full, 0);
+        for (int j = 0; ok && j < n; ++j) {
+          const int st = j % STAGES;
+          if (!wait(&k_full[st], (j / STAGES) & 1)) break;
           for (int t = 0; t < n_tiles; ++t) {
-            if (!wait(&s_free[t], j & 1)) {
+            // S_t(j) once the softmax has taken S_t(j-1) into registers.
+            if (j > 0 && !wait(&s_free[t], (j - 1) & 1)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            issue_qk(t, st1);
+            issue_qk(t, st);
             commit(&s_full[t]);
           }
-          if (!ok) break;
         }
-        if (!wait(&v_full[st], (j / STAGES) & 1)) break;
-        for (int t = 0; t < n_tiles; ++t) {
-          if (!wait(&p_full[2 * t + buf], (j >> 1) & 1)) {
-            ok = false;
-            break;
+        commit(&drain[0]);  // no MMA of this warp may be in flight when TMEM is released
+        mbar_wait(&drain[0], 0, p.status, nullptr);
+      } else {
+        auto issue_pv = [&](int t, int st, int buf, bool accumulate) {
+          // O_t += P_t[buf] . V over 64 keys in steps of 16 keys (8 TMEM columns of P, 2048 bytes of V).
+          const uint32_t a = tmem + L::COL_P + 64 * t + 32 * buf;
+          const uint64_t vb = dv0 + (uint64_t)((st * L::KV_TILE) >> 4);
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            if (leader)
+              umma_f16_ts(tmem + t * D, a + ks * 8, vb + (uint64_t)((ks * 2048) >> 4), idesc_pv,
+                          (accumulate || ks > 0) ? 1u : 0u);
+            __syncwarp();
           }
-          tc_fence_after();
-          issue_pv(t, st, buf, j > 0);
-          commit(&o_done[2 * t + buf]);
+        };
+        for (int j = 0; ok && j < n; ++j) {
+          const int st = j % STAGES;
+          const int buf = j & 1;
+          if (!wait(&v_full[st], (j / STAGES) & 1)) break;
+          for (int t = 0; t < n_tiles; ++t) {
+            if (!wait(&p_full[2 * t + buf], (j >> 1) & 1)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_pv(t, st, buf, j > 0);
+            commit(&o_done[2 * t + buf]);
+          }
+          if (!ok) break;
+          // QK(j) finished before softmax(j) began, so PV(j) completing frees stage st.
+          commit(&kv_empty[st]);
         }
-        if (!ok) break;
-        commit(&kv_empty[st]);
+        commit(&drain[1]);
+        mbar_wait(&drain[1], 0, p.status, nullptr);
       }
-      // No MMA may be in flight when TMEM is released.
-      commit(drain);
-      mbar_wait(drain, 0, p.status, nullptr);
     }
     __syncwarp();
   } else {
