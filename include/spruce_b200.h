@@ -132,6 +132,31 @@ SPRUCE_API int spruce_select_blocks(const void *q, const int64_t q_strides[4], c
                          void *stream);
 
 /*
+ * spruce_select_blocks without a caller workspace; it has no counterpart in
+ * the reference.  It exists for callers that cannot allocate device memory for
+ * us: hosts that reserve the GPU's memory up front in their own pool (a
+ * serving process that hands nearly all HBM to its KV cache at start-up) and
+ * plugin bindings that pass only the input and output buffers they own.
+ * Scratch comes from one static device array of
+ * spruce_select_noalloc_max_scratch_bytes() bytes (16 MiB) that every GPU
+ * loading this library holds until the process exits; shapes needing more
+ * (spruce_select_workspace_bytes) are rejected with SPRUCE_ERR_UNSUPPORTED.
+ * No cudaMalloc, cudaFree or allocating library routine is called.  The first
+ * call on a device looks up the array's device address (cudaGetSymbolAddress)
+ * with that device current; make that first call before any stream capture.
+ * All calls share the one array: calls that overlap on the GPU (different
+ * streams, or other host threads) race on it; serialise them.
+ */
+SPRUCE_API int spruce_select_blocks_noalloc(const void *q, const int64_t q_strides[4], const void *k,
+                                            const int64_t k_strides[4], int dtype, int64_t B, int64_t Hq,
+                                            int64_t Hkv, int64_t T, int64_t D, const float *Wq, const float *Wk,
+                                            int64_t P, int64_t K, int64_t local_window, int64_t sink_blocks,
+                                            int32_t *out, const int64_t out_strides[3], void *stream);
+
+/* Size of the static scratch array spruce_select_blocks_noalloc uses. */
+SPRUCE_API int64_t spruce_select_noalloc_max_scratch_bytes(void);
+
+/*
  * selected_ids_to_blocks, scripts/export_selected_blocks.py:80-175:
  * ids [R, qb, C] int64 (R = layers x groups, contiguous) -> out [R, qb, K]
  * int32.  Same policy: forced local window and sink blocks, deduplicated

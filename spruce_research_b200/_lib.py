@@ -42,6 +42,9 @@ SIGNATURES = {
     "spruce_select_workspace_bytes": ([_I64, _I64, _I64, _I64, _I64, _INT], _I64),
     "spruce_select_blocks": ([_P, _P, _P, _P, _INT, _I64, _I64, _I64, _I64, _I64, _P, _P, _I64, _I64, _I64,
                               _I64, _P, _P, _P, _I64, _P], _INT),
+    "spruce_select_blocks_noalloc": ([_P, _P, _P, _P, _INT, _I64, _I64, _I64, _I64, _I64, _P, _P, _I64, _I64,
+                                      _I64, _I64, _P, _P, _P], _INT),
+    "spruce_select_noalloc_max_scratch_bytes": ([], _I64),
     "spruce_pack_selected_ids": ([_P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P], _INT),
     "spruce_validate_selected_blocks": ([_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P], _INT),
     "spruce_sparse_attention_fwd": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _INT, _I64, _I64, _I64, _I64, _I64,

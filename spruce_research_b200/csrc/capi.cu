@@ -7,6 +7,7 @@
 // allocates device memory or synchronises.
 #include <cstdarg>
 #include <cstdio>
+#include <mutex>
 #include <string>
 
 #include "common.cuh"
@@ -193,6 +194,66 @@ int spruce_select_blocks(const void* q, const int64_t q_strides[4], const void* 
   rc = spruce_gate_project(pooled_k, dtype, rows, D, Wk, P, kp, stream);
   if (rc) return rc;
   return spruce_gate_select(qp, kp, B, Hkv, qb, P, K, local_window, sink_blocks, out, out_strides, stream);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------- no-allocation selector
+// Scratch for spruce_select_blocks_noalloc: one file-scope device array that
+// every GPU loading this library holds until the process exits.  In host code
+// `g_select_scratch` is only a host-side stand-in, never a device address; the
+// device address is fetched per device with cudaGetSymbolAddress below.
+namespace {
+
+constexpr int64_t kNoAllocScratchBytes = int64_t(16) << 20;  // 16 MiB
+static __device__ __align__(256) unsigned char g_select_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_addr[kMaxDevices] = {};
+
+// Device address of g_select_scratch on the current device, looked up once per
+// device (the first call on a device does this; it makes no allocation).
+int scratch_for_current_device(void** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(SPRUCE_ERR_UNSUPPORTED, "device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_addr[dev] == nullptr) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_select_scratch);
+    if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(g_select_scratch)");
+    g_scratch_addr[dev] = ptr;
+  }
+  *out = g_scratch_addr[dev];
+  return SPRUCE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int64_t spruce_select_noalloc_max_scratch_bytes(void) { return kNoAllocScratchBytes; }
+
+int spruce_select_blocks_noalloc(const void* q, const int64_t q_strides[4], const void* k, const int64_t k_strides[4],
+                                 int dtype, int64_t B, int64_t Hq, int64_t Hkv, int64_t T, int64_t D, const float* Wq,
+                                 const float* Wk, int64_t P, int64_t K, int64_t local_window, int64_t sink_blocks,
+                                 int32_t* out, const int64_t out_strides[3], void* stream) {
+  if (!valid_dtype(dtype)) return fail(SPRUCE_ERR_INVALID, "unsupported dtype code %d", dtype);
+  const int64_t need = spruce_select_workspace_bytes(B, Hkv, T, D, P, dtype);
+  if (need > kNoAllocScratchBytes)
+    return fail(SPRUCE_ERR_UNSUPPORTED,
+                "spruce_select_blocks_noalloc: this shape needs %lld bytes of scratch, more than the %lld-byte "
+                "static buffer; use spruce_select_blocks with a caller-provided workspace",
+                (long long)need, (long long)kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  int rc = scratch_for_current_device(&scratch);
+  if (rc) return rc;
+  // Every region the selector reads (pooled features, projections) is fully
+  // written earlier in the same call, so nothing needs clearing first.
+  return spruce_select_blocks(q, q_strides, k, k_strides, dtype, B, Hq, Hkv, T, D, Wq, Wk, P, K, local_window,
+                              sink_blocks, out, out_strides, scratch, kNoAllocScratchBytes, stream);
 }
 
 int spruce_pack_selected_ids(const int64_t* ids, int64_t R, int64_t qb, int64_t C, int64_t K, int64_t local_window,
