@@ -75,13 +75,15 @@ class ShardedSparsePrefill:
         s = self.shard
         world = s.world
         chunk = chunk.contiguous()
-        if self._gathered is None or self._gathered.shape[1:] != chunk.shape:
-            self._gathered = torch.empty((world, *chunk.shape), device=chunk.device, dtype=chunk.dtype)
-        dist.all_gather_into_tensor(self._gathered, chunk, group=self.group)
         B, Tc, Hr, D = chunk.shape
+        if self._gathered is None or self._gathered.shape != (world * B, Tc, Hr, D):
+            self._gathered = torch.empty((world * B, Tc, Hr, D), device=chunk.device, dtype=chunk.dtype)
+        # rank-major concatenation along dim 0 (the form both NCCL and gloo accept)
+        dist.all_gather_into_tensor(self._gathered, chunk, group=self.group)
+        gathered = self._gathered.view(world, B, Tc, Hr, D)
         if s.parts == 1:
             # [world, B, T, Hq/world, D] -> [B, T, Hq, D]
-            return self._gathered.permute(1, 2, 0, 3, 4).reshape(B, tokens, world * Hr, D)
+            return gathered.permute(1, 2, 0, 3, 4).reshape(B, tokens, world * Hr, D)
         # rank = g * parts + p: [G, parts, B, T/parts, rep, D] -> [B, parts, T/parts, G, rep, D]
-        x = self._gathered.view(kv_heads, s.parts, B, Tc, Hr, D).permute(2, 1, 3, 0, 4, 5)
+        x = gathered.view(kv_heads, s.parts, B, Tc, Hr, D).permute(2, 1, 3, 0, 4, 5)
         return x.reshape(B, tokens, kv_heads * Hr, D)

@@ -1,0 +1,99 @@
+"""Host-side logic: C-ABI library, argument checks, synthetic workload maths, sharding.
+
+No GPU compute runs here: the library is loaded and exercised only on paths
+that reject arguments before touching the device.
+"""
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+from spruce_research_b200 import _lib, native
+from spruce_research_b200.sharding import plan
+from spruce_research_b200.synthetic import (LayerShape, causal_block_entries, k_for_density, make_gate_weights,
+                                            make_layer_inputs, sparse_attention_flops)
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_symbols():
+    text = open(os.path.join(ROOT, "include", "spruce_b200.h")).read()
+    return sorted(set(re.findall(r"SPRUCE_API\s+[\w\s\*]*?\b(spruce_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_header_symbol():
+    L = _lib.load()
+    names = header_symbols()
+    assert len(names) >= 15
+    for name in names:
+        assert hasattr(L, name), f"{name} declared in include/spruce_b200.h but not exported"
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+    assert L.spruce_abi_version() == 1
+
+
+def test_policy_errors_are_value_errors_before_any_device_work():
+    L = _lib.load()
+    out3 = _lib.int64s(0, 0, 0)
+    rc = L.spruce_gate_select(None, None, 1, 1, 4, 8, 2, 1, 1, None, out3, None)  # K=2 < lw+1+sink=3
+    assert rc == _lib.ERR_INVALID
+    with pytest.raises(ValueError, match="cannot fit local window size 2 plus 1 sink"):
+        _lib.check(rc)
+    s4 = _lib.int64s(1, 1, 1, 1)
+    rc = L.spruce_sparse_attention_fwd(None, s4, None, s4, None, s4, None, s4, None, s4, 1, 1, 2, 1, 64, 96, 3,
+                                       0.1, None, None)
+    with pytest.raises(ValueError, match="head_dim 64 or 128"):
+        _lib.check(rc)
+    rc = L.spruce_pack_selected_ids(None, 1, 4, 2, 3, 1, 0, 0, None, None)
+    with pytest.raises(ValueError, match="key_blocks"):
+        _lib.check(rc)
+
+
+def test_cpu_tensors_are_rejected_without_fallback():
+    x = torch.zeros(1, 2, 64, 64, dtype=torch.bfloat16)
+    idx = torch.zeros(1, 1, 1, 1, dtype=torch.int32)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        native.sparse_attention(x, x[:, :1], x[:, :1], idx)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        native.pool_qk(x, x[:, :1])
+
+
+def test_density_k_and_flops_match_the_survey_figures():
+    assert k_for_density(512, 0.10) == 27 and causal_block_entries(512, 27) == 13473
+    assert k_for_density(2048, 0.10) == 106 and causal_block_entries(2048, 106) == 211523
+    assert k_for_density(1024, 0.10) == 53
+    assert [k_for_density(2048, d) for d in (0.02, 0.05, 0.25, 0.50, 1.0)] == [21, 52, 275, 600, 2048]
+    flops = sparse_attention_flops(LayerShape(1, 28, 4, 131072, 128), 211523)
+    assert abs(flops - 12.3615e12) / 12.3615e12 < 1e-3
+    assert abs(sparse_attention_flops(LayerShape(1, 28, 4, 32768, 128), 13473) - 0.776e12) < 1e9
+
+
+def test_synthetic_inputs_are_seeded_and_strided_like_hf():
+    shape = LayerShape(1, 4, 2, 130, 64)
+    a = make_layer_inputs(shape, torch.bfloat16, seed=5)
+    b = make_layer_inputs(shape, torch.bfloat16, seed=5)
+    for x, y in zip(a, b):
+        assert torch.equal(x, y)
+        assert x.shape[2] == 130 and not x.is_contiguous()       # [B, H, T, D] view of [B, T, H, D]
+    wq, wk = make_gate_weights(1, 64, 64, seed=1)
+    assert wq.abs().max() <= 1 / 64 and wk.shape == (1, 64, 64)
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_shard_plan_covers_every_group_and_block_once(world):
+    Hkv, qb = 4, 2048
+    seen = torch.zeros(Hkv, qb, dtype=torch.int32)
+    for r in range(world):
+        s = plan(world, r, Hkv, qb)
+        g0, g1 = s.groups
+        i0, i1 = s.q_blocks
+        seen[g0:g1, i0:i1] += 1
+    assert torch.equal(seen, torch.ones_like(seen))
+
+
+def test_shard_plan_rejects_uneven_splits():
+    with pytest.raises(ValueError):
+        plan(3, 0, 4, 2048)
+    with pytest.raises(ValueError):
+        plan(8, 0, 4, 2047)

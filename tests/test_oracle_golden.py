@@ -1,0 +1,110 @@
+"""The CPU oracle against the reference's own outputs (tests/golden/, made by make_golden.py).
+
+This pins the oracle: every later GPU parity claim is "CUDA == oracle" plus
+"oracle == reference" from here.  Runs on CPU.
+"""
+import numpy as np
+import pytest
+import torch
+
+from golden_cases import CASE_NAMES, DT, from_raw, load_case, load_npz
+from oracle import oracle as O
+
+
+@pytest.mark.parametrize("name", CASE_NAMES)
+def test_pooled_features_bit_exact(name):
+    case = load_case(name)
+    q, k, v, wq, wk = case.inputs()
+    r = O.select_blocks(q, k, wq, wk, case.K, case.local_window, case.sink)
+    assert torch.equal(r["pooled_q"], case.golden("pooled_q"))
+    assert torch.equal(r["pooled_k"], case.golden("pooled_k"))
+
+
+@pytest.mark.parametrize("name", CASE_NAMES)
+def test_selected_blocks_bit_exact_and_scores_close(name):
+    case = load_case(name)
+    q, k, v, wq, wk = case.inputs()
+    r = O.select_blocks(q, k, wq, wk, case.K, case.local_window, case.sink)
+    # fixed-order fma vs MKL: a few fp32 ulps
+    assert (r["scores"] - case.golden("scores")).abs().max().item() < 1e-8
+    assert torch.equal(r["selected"], case.golden("selected"))
+    O.validate_selected_blocks(r["selected"][:, None].contiguous(), local_window=case.local_window)
+
+
+@pytest.mark.parametrize("name", CASE_NAMES)
+def test_attention_matches_reference(name):
+    case = load_case(name)
+    q, k, v, wq, wk = case.inputs()
+    out = O.sparse_attention(q, k, v, case.golden("selected"), out_dtype=torch.float32)
+    rows = case.out_rows()
+    err = (out[:, rows] - case.golden("out").float()).abs()
+    if case.dtype == torch.float32:
+        assert err.max().item() < 1e-5
+    else:
+        # the golden is rounded to the input dtype: within one ulp of |x| <= 8
+        assert err.max().item() < 1.6e-2
+        assert err.mean().item() < 1e-3
+
+
+def test_packing_matches_reference():
+    z = load_npz("packing")
+    n = 0
+    while f"pack{n}_ids" in z:
+        K, lw, kb, sink = (int(x) for x in z[f"pack{n}_args"])
+        got = O.selected_ids_to_blocks(torch.from_numpy(z[f"pack{n}_ids"]), K, lw, kb, sink)
+        assert torch.equal(got, torch.from_numpy(z[f"pack{n}_out"])), f"packing case {n}"
+        n += 1
+    assert n == 6
+
+
+def test_mean_prototype_matches_reference():
+    z = load_npz("proto")
+    for n in range(3):
+        dt = DT[int(z[f"proto{n}_dtype"][0])]
+        x = from_raw(z[f"proto{n}_x"], dt)
+        got = O.proto_pool_seq(x, 64, 1)
+        want = from_raw(z[f"proto{n}_p1"], dt)
+        assert torch.equal(got, want), f"proto case {n}"
+
+
+def test_validator_messages_follow_reference():
+    def row(ids, k=4):
+        return list(ids) + [-1] * (k - len(ids))
+
+    ok = torch.tensor([[[[row([0]), row([0, 1]), row([0, 1, 2]), row([0, 2, 3])]]]], dtype=torch.int32)
+    O.validate_selected_blocks(ok)
+    cases = [  # rows of one (batch, layer, group), as in tests/test_validator.py of the reference
+        ([row([0, 5])], "future"),
+        ([row([0]), row([0, 1, 1])], "Duplicate"),
+        ([row([0]), row([0, 1]), row([0, 2, 1])], "Not sorted"),
+        ([row([0]), row([1])], "Missing local-window"),
+        ([row([0]), [0, -1, 1, -1]], "trailing"),
+    ]
+    for rows, msg in cases:
+        with pytest.raises(AssertionError, match=msg):
+            O.validate_selected_blocks(torch.tensor([[[rows]]], dtype=torch.int32))
+
+
+def test_dense_reference_equals_all_block_oracle():
+    # 100% density: the block-sparse oracle must equal dense causal attention.
+    from spruce_research_b200.synthetic import LayerShape, make_layer_inputs
+
+    shape = LayerShape(1, 4, 2, 200, 64)
+    q, k, v = make_layer_inputs(shape, torch.float32, seed=3)
+    qb = shape.query_blocks
+    idx = torch.full((1, 2, qb, qb), -1, dtype=torch.int32)
+    for i in range(qb):
+        idx[0, :, i, : i + 1] = torch.arange(i + 1, dtype=torch.int32)
+    sparse = O.sparse_attention(q, k, v, idx, out_dtype=torch.float32)
+    dense = O.dense_causal_attention(q, k, v)
+    assert (sparse - dense).abs().max().item() < 1e-5
+
+
+def test_golden_fixtures_are_small():
+    import os
+
+    from golden_cases import HERE
+
+    total = sum(os.path.getsize(os.path.join(HERE, f)) for f in os.listdir(HERE) if f.endswith(".npz"))
+    assert total < 6 * 2**20
+    assert np.load(os.path.join(HERE, "c0.npz"))["selected"].dtype == np.int32
