@@ -52,6 +52,8 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target length of one CPU sample")
+    ap.add_argument("--gather", choices=("fused", "nccl"), default="fused",
+                    help="N>1 output all-gather: NVLink peer stores in the attention epilogue, or NCCL")
     return ap.parse_args()
 
 
@@ -150,6 +152,9 @@ def workload(args):
 
 def config_dict(args, shape, K, entries, world):
     par = {1: "single GPU", 2: "kv-group x2", 4: "kv-group x4", 8: "half kv-group x8"}.get(world, f"x{world}")
+    if world > 1:
+        par += (", output all-gather fused into the attention epilogue (NVLink peer stores)"
+                if args.gather == "fused" else ", NCCL all_gather")
     return {
         "workload": (f"config 2: one Qwen2.5-7B-shaped attention layer, {shape.tokens} tokens, "
                      f"{shape.q_heads}Q/{shape.kv_heads}KV heads, d={shape.head_dim}, bf16, "
@@ -225,7 +230,7 @@ def run_b200(args):
 
     from spruce_research_b200 import native
     from spruce_research_b200.pipeline import SparsePrefillLayer
-    from spruce_research_b200.sharding import ShardedSparsePrefill, plan
+    from spruce_research_b200.sharding import PeerOutput, ShardedSparsePrefill, plan
     from spruce_research_b200.synthetic import make_gate_weights, make_layer_inputs
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -249,8 +254,18 @@ def run_b200(args):
     rep = shape.q_heads // shape.kv_heads
     i0, i1 = shard.q_blocks
     B, T, D = shape.batch, shape.tokens, shape.head_dim
-    local_out = torch.empty((B, T, (g1 - g0) * rep, D), device=dev, dtype=torch.bfloat16)
     sel_buf = torch.empty((B, g1 - g0, qb, K), device=dev, dtype=torch.int32)
+    fused = world > 1 and args.gather == "fused"
+    peer = None
+    if fused:
+        # every rank's full output is mapped into every other rank; this rank's heads are a view
+        peer = PeerOutput((B, T, shape.q_heads, D), torch.bfloat16, dev)
+        local_out = peer.local[:, :, g0 * rep:g1 * rep]
+        view_bytes = local_out.storage_offset() * local_out.element_size()
+        peer_ptrs = [ptr + view_bytes for ptr in peer.peer_ptrs]
+    else:
+        local_out = torch.empty((B, T, (g1 - g0) * rep, D), device=dev, dtype=torch.bfloat16)
+        peer_ptrs = None
 
     def step(qs, ks, vs, marks=None):
         """This rank's selector + attention (+ all-gather); q/k/v are its shard's views."""
@@ -259,11 +274,14 @@ def run_b200(args):
         sel = layer.select(qs, ks, out=sel_buf)
         if marks is not None:
             marks[1].record()
-        native.sparse_attention(qs, ks, vs, sel, out=local_out, q_blocks=(i0, i1))
+        native.sparse_attention(qs, ks, vs, sel, out=local_out, q_blocks=(i0, i1), peer_outs=peer_ptrs)
         if marks is not None:
             marks[2].record()
         full = local_out
-        if world > 1:
+        if fused:
+            peer.fence()
+            full = peer.local
+        elif world > 1:
             full = runner.gather(local_out[:, i0 * 64:i1 * 64], shape.kv_heads, T)
         if marks is not None:
             marks[3].record()
@@ -359,7 +377,8 @@ def run_b200(args):
         "dtype": "bf16",
         "data": "synthetic: seeded N(0,1) Q/K/V, RoPE base 1e6, planted affinity (3 blocks/query block)",
         "config": config_dict(args, shape, K, entries, world),
-        "breakdown_ms": {"selector": sel_ms_max, "attention": attn_ms_max, "gather": gather_ms_max},
+        "breakdown_ms": {"selector": sel_ms_max, "attention": attn_ms_max,
+                         ("fence" if fused else "gather"): gather_ms_max},
         "roofline": {"bound": "tensor", "kernel": "attn_fwd_sm100_kernel<bf16,128,3>",
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                      "peak_source": peak_src + ", of measured",
@@ -375,6 +394,10 @@ def run_b200(args):
         print(json.dumps(result), flush=True)
     if world > 1:
         dist.barrier(device_ids=[local])
+        if peer is not None:
+            torch.cuda.synchronize()
+            peer.close()
+            dist.barrier(device_ids=[local])
         dist.destroy_process_group()
 
 

@@ -212,6 +212,40 @@ SPRUCE_API int spruce_sparse_attention_fwd_rows(const void *q, const int64_t q_s
                                                 int64_t q_block_begin, int64_t q_block_end, uint32_t *status,
                                                 void *stream);
 
+/*
+ * spruce_sparse_attention_fwd_rows with the output all-gather fused into the
+ * kernel's epilogue, for layers whose query heads are split across GPUs (the
+ * NCCL all-gather of per-head outputs of SURVEY multi-GPU plan, done as
+ * NVLink peer stores while the attention runs).  Each output row is written to
+ * `out` and, at the same element offset, to every `peer_outs[i]` (n_peers <=
+ * 7): device pointers of identically laid out tensors on the other GPUs,
+ * mapped into this process (CUDA IPC) with peer access.  Plain stores; no
+ * multicast.  The caller orders the peers' reads after every rank's kernel
+ * (e.g. a collective on the same stream).  bf16/fp16 only.
+ */
+SPRUCE_API int spruce_sparse_attention_fwd_scatter(const void *q, const int64_t q_strides[4], const void *k,
+                                                   const int64_t k_strides[4], const void *v,
+                                                   const int64_t v_strides[4], const int32_t *indices,
+                                                   const int64_t idx_strides[4], void *out,
+                                                   const int64_t out_strides[4], int dtype, int64_t B, int64_t Hq,
+                                                   int64_t Hkv, int64_t T, int64_t D, int64_t Kw, float scale,
+                                                   int64_t q_block_begin, int64_t q_block_end,
+                                                   const void *const *peer_outs, int32_t n_peers, uint32_t *status,
+                                                   void *stream);
+
+/*
+ * Host-only CUDA IPC plumbing for the fused output all-gather (no counterpart
+ * in the reference, which is single-GPU).  spruce_ipc_export writes the
+ * 64-byte cudaIpcMemHandle of the allocation holding `ptr` to `handle` and
+ * ptr's byte offset in it; spruce_ipc_import opens a peer's handle in the
+ * CURRENT device's context with lazy peer access and returns the mapped
+ * pointer (base + offset) and the mapping base for spruce_ipc_close.  They map
+ * existing memory; nothing is allocated.
+ */
+SPRUCE_API int spruce_ipc_export(const void *ptr, void *handle, int64_t *offset);
+SPRUCE_API int spruce_ipc_import(const void *handle, int64_t offset, void **ptr, void **base);
+SPRUCE_API int spruce_ipc_close(void *base);
+
 #ifdef __cplusplus
 }
 #endif

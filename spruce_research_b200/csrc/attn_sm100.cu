@@ -56,6 +56,8 @@ struct AttnParams {
   int q_begin, nq;  // query blocks [q_begin, q_begin + nq) are computed
   float scale_log2;
   uint32_t* status;
+  void* peer_out[kMaxPeers];  // fused output all-gather targets (NVLink peer memory)
+  int n_peer;
 };
 
 template <int D, int STAGES>
@@ -424,7 +426,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const int hh = 2 * (pair0 + t) + (row & 1);
       const int token = i * 64 + tok;
       const bool valid = hh < p.rep && token < p.T;
-      T* orow = static_cast<T*>(p.out) + b * p.osb + (int64_t)(g * p.rep + hh) * p.osh + (int64_t)token * p.ost;
+      const int64_t orow_off = b * p.osb + (int64_t)(g * p.rep + hh) * p.osh + (int64_t)token * p.ost;
+      T* orow = static_cast<T*>(p.out) + orow_off;
       const float inv = l > 0.0f ? 1.0f / l : 0.0f;
       if (n == 0 && row == 0) raise_status(p.status, SPRUCE_STATUS_EMPTY_ROW);
 #pragma unroll 1
@@ -446,6 +449,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             v.z = Pack2<T>::pack(o[v4 * 8 + 4] * inv, o[v4 * 8 + 5] * inv);
             v.w = Pack2<T>::pack(o[v4 * 8 + 6] * inv, o[v4 * 8 + 7] * inv);
             *reinterpret_cast<uint4*>(orow + cc * 32 + v4 * 8) = v;
+            // Fused all-gather: the same row into every peer's output over NVLink.
+            for (int pp = 0; pp < p.n_peer; ++pp)
+              *reinterpret_cast<uint4*>(static_cast<T*>(p.peer_out[pp]) + orow_off + cc * 32 + v4 * 8) = v;
           }
         }
       }
@@ -520,6 +526,8 @@ static cudaError_t launch_typed(const AttnArgs& a, CUtensorMapDataType dt, cudaS
   p.n_cta = (p.n_pair + 1) / 2;
   p.scale_log2 = a.scale * 1.4426950408889634f;
   p.status = a.status;
+  p.n_peer = a.n_peer;
+  for (int pp = 0; pp < kMaxPeers; ++pp) p.peer_out[pp] = pp < a.n_peer ? const_cast<void*>(a.peer_out[pp]) : nullptr;
   const size_t smem = L::smem_bytes(a.Kw);
   auto kern = attn_fwd_sm100_kernel<T, D, STAGES>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

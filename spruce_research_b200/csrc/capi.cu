@@ -7,6 +7,7 @@
 // allocates device memory or synchronises.
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 #include <string>
 
@@ -51,6 +52,15 @@ cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 }  // namespace
 
 extern "C" {
+static int spruce_sparse_attention_fwd_rows_impl(const void* q, const int64_t q_strides[4], const void* k,
+                                                 const int64_t k_strides[4], const void* v,
+                                                 const int64_t v_strides[4], const int32_t* indices,
+                                                 const int64_t idx_strides[4], void* out,
+                                                 const int64_t out_strides[4], int dtype, int64_t B, int64_t Hq,
+                                                 int64_t Hkv, int64_t T, int64_t D, int64_t Kw, float scale,
+                                                 int64_t q_block_begin, int64_t q_block_end,
+                                                 const void* const* peer_outs, int n_peers, uint32_t* status,
+                                                 void* stream);
 
 const char* spruce_last_error(void) { return g_last_error.c_str(); }
 
@@ -256,6 +266,49 @@ int spruce_select_blocks_noalloc(const void* q, const int64_t q_strides[4], cons
                               sink_blocks, out, out_strides, scratch, kNoAllocScratchBytes, stream);
 }
 
+// ---------------------------------------------------------------- CUDA IPC plumbing (host only)
+using GetAddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+static GetAddressRangeFn address_range_fn() {
+  static GetAddressRangeFn fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<GetAddressRangeFn>(ptr);
+  }
+  return fn;
+}
+
+int spruce_ipc_export(const void* ptr, void* handle, int64_t* offset) {
+  GetAddressRangeFn range = address_range_fn();
+  if (range == nullptr) return fail(SPRUCE_ERR_CUDA, "cuMemGetAddressRange is unavailable");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return fail(SPRUCE_ERR_INVALID, "pointer is not inside a device allocation");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return cuda_status(e, "cudaIpcGetMemHandle");
+  memcpy(handle, &h, sizeof(h));
+  *offset = static_cast<int64_t>(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  return SPRUCE_OK;
+}
+
+int spruce_ipc_import(const void* handle, int64_t offset, void** ptr, void** base) {
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* b = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&b, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_status(e, "cudaIpcOpenMemHandle");
+  *base = b;
+  *ptr = static_cast<uint8_t*>(b) + offset;
+  return SPRUCE_OK;
+}
+
+int spruce_ipc_close(void* base) { return cuda_status(cudaIpcCloseMemHandle(base), "cudaIpcCloseMemHandle"); }
+
 int spruce_pack_selected_ids(const int64_t* ids, int64_t R, int64_t qb, int64_t C, int64_t K, int64_t local_window,
                              int64_t key_blocks, int64_t sink_blocks, int32_t* out, void* stream) {
   int rc = check_select_policy(K, local_window, sink_blocks);
@@ -278,12 +331,43 @@ int spruce_validate_selected_blocks(const int32_t* sel, int64_t B, int64_t L, in
                      "validate launch");
 }
 
+int spruce_sparse_attention_fwd_scatter(const void* q, const int64_t q_strides[4], const void* k,
+                                        const int64_t k_strides[4], const void* v, const int64_t v_strides[4],
+                                        const int32_t* indices, const int64_t idx_strides[4], void* out,
+                                        const int64_t out_strides[4], int dtype, int64_t B, int64_t Hq,
+                                        int64_t Hkv, int64_t T, int64_t D, int64_t Kw, float scale,
+                                        int64_t q_block_begin, int64_t q_block_end, const void* const* peer_outs,
+                                        int32_t n_peers, uint32_t* status, void* stream) {
+  if (n_peers < 0 || n_peers > spruce::kMaxPeers)
+    return fail(SPRUCE_ERR_UNSUPPORTED, "n_peers=%d outside [0, %d]", (int)n_peers, spruce::kMaxPeers);
+  if (n_peers > 0 && dtype == SPRUCE_DTYPE_F32)
+    return fail(SPRUCE_ERR_UNSUPPORTED, "the fused output all-gather covers the bf16/fp16 kernel only");
+  for (int i = 0; i < n_peers; ++i)
+    if (peer_outs[i] == nullptr || !aligned16(peer_outs[i]))
+      return fail(SPRUCE_ERR_INVALID, "peer output %d must be a 16-byte aligned device pointer", i);
+  return spruce_sparse_attention_fwd_rows_impl(q, q_strides, k, k_strides, v, v_strides, indices, idx_strides, out,
+                                               out_strides, dtype, B, Hq, Hkv, T, D, Kw, scale, q_block_begin,
+                                               q_block_end, peer_outs, n_peers, status, stream);
+}
+
 int spruce_sparse_attention_fwd_rows(const void* q, const int64_t q_strides[4], const void* k,
                                      const int64_t k_strides[4], const void* v, const int64_t v_strides[4],
                                      const int32_t* indices, const int64_t idx_strides[4], void* out,
                                      const int64_t out_strides[4], int dtype, int64_t B, int64_t Hq, int64_t Hkv,
                                      int64_t T, int64_t D, int64_t Kw, float scale, int64_t q_block_begin,
                                      int64_t q_block_end, uint32_t* status, void* stream) {
+  return spruce_sparse_attention_fwd_rows_impl(q, q_strides, k, k_strides, v, v_strides, indices, idx_strides, out,
+                                               out_strides, dtype, B, Hq, Hkv, T, D, Kw, scale, q_block_begin,
+                                               q_block_end, nullptr, 0, status, stream);
+}
+
+static int spruce_sparse_attention_fwd_rows_impl(const void* q, const int64_t q_strides[4], const void* k,
+                                     const int64_t k_strides[4], const void* v, const int64_t v_strides[4],
+                                     const int32_t* indices, const int64_t idx_strides[4], void* out,
+                                     const int64_t out_strides[4], int dtype, int64_t B, int64_t Hq, int64_t Hkv,
+                                     int64_t T, int64_t D, int64_t Kw, float scale, int64_t q_block_begin,
+                                     int64_t q_block_end, const void* const* peer_outs, int n_peers,
+                                     uint32_t* status, void* stream) {
   if (!valid_dtype(dtype)) return fail(SPRUCE_ERR_INVALID, "unsupported dtype code %d", dtype);
   if (D != 64 && D != 128) return fail(SPRUCE_ERR_INVALID, "kernel supports head_dim 64 or 128, got %lld", (long long)D);
   if (B < 0 || Hq < 1 || Hkv < 1 || T < 0 || Kw < 0) return fail(SPRUCE_ERR_INVALID, "bad attention shape");
@@ -299,7 +383,7 @@ int spruce_sparse_attention_fwd_rows(const void* q, const int64_t q_strides[4], 
     return fail(SPRUCE_ERR_UNSUPPORTED, "shape too large for the launch grid");
   spruce::AttnArgs a{q, k, v, q_strides, k_strides, v_strides, indices, idx_strides, out, out_strides,
                      (int)B, (int)Hq, (int)Hkv, (int)T, (int)D, (int)Kw, scale, status,
-                     (int)q_block_begin, (int)q_block_end};
+                     (int)q_block_begin, (int)q_block_end, peer_outs, n_peers};
   if (dtype == SPRUCE_DTYPE_F32) {
     if (Kw > 8192) return fail(SPRUCE_ERR_UNSUPPORTED, "row width %lld too large", (long long)Kw);
     return cuda_status(spruce::launch_attn_f32(a, as_stream(stream)), "fp32 attention launch");

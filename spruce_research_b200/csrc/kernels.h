@@ -47,7 +47,13 @@ struct AttnArgs {
   float scale;
   uint32_t* status;
   int q_begin, q_end;  // query-block range to compute
+  // Fused output all-gather: every output row is also stored at the same
+  // offset in each of these peer buffers (P2P-mapped, identical layout).
+  const void* const* peer_out;
+  int n_peer;
 };
+
+constexpr int kMaxPeers = 7;
 
 // tcgen05 path (bf16 / fp16).  Returns cudaErrorInvalidValue for shapes it
 // does not cover (the C ABI checks them first).

@@ -8,6 +8,7 @@ layers over these.
 """
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -193,12 +194,16 @@ def validate_first_violation(sel: torch.Tensor, local_window: int) -> tuple[int,
 
 def sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices: torch.Tensor,
                      scale: float | None = None, out: torch.Tensor | None = None,
-                     status: torch.Tensor | None = None, q_blocks: tuple[int, int] | None = None) -> torch.Tensor:
+                     status: torch.Tensor | None = None, q_blocks: tuple[int, int] | None = None,
+                     peer_outs: list[int] | None = None) -> torch.Tensor:
     """Block-sparse causal GQA attention -> token-major [B, T, Hq, D].
 
     q [B, Hq, T, D], k/v [B, Hkv, T, D] (strided views are fine),
     indices int32 [B, Hkv, ceil(T/64), K].  With ``q_blocks=(i0, i1)`` only
-    query blocks i0..i1-1 are computed (their rows of ``out``).
+    query blocks i0..i1-1 are computed (their rows of ``out``).  With
+    ``peer_outs`` (device pointers of other GPUs' identically laid out output
+    tensors, mapped into this process) every row is also stored there: the
+    output all-gather fused into the kernel.
     """
     _lib.require_cuda(q, k, v, indices)
     B, Hq, T, D = q.shape
@@ -217,6 +222,14 @@ def sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices:
     ostr = _lib.int64s(out.stride(0), out.stride(2), out.stride(1), out.stride(3))
     i0, i1 = (0, qb) if q_blocks is None else q_blocks
     L = _lib.load()
+    if peer_outs:
+        peers = (ctypes.c_void_p * len(peer_outs))(*peer_outs)
+        _lib.check(L.spruce_sparse_attention_fwd_scatter(
+            q.data_ptr(), _lib.strides(q), k.data_ptr(), _lib.strides(k), v.data_ptr(), _lib.strides(v),
+            indices.data_ptr(), _lib.strides(indices), out.data_ptr(), ostr, _dt(q), B, Hq, Hkv, T, D,
+            indices.shape[-1], float(scale), i0, i1, peers, len(peer_outs),
+            status.data_ptr() if status is not None else None, _lib.stream_of(q)))
+        return out
     _lib.check(L.spruce_sparse_attention_fwd_rows(
         q.data_ptr(), _lib.strides(q), k.data_ptr(), _lib.strides(k), v.data_ptr(), _lib.strides(v),
         indices.data_ptr(), _lib.strides(indices), out.data_ptr(), ostr, _dt(q), B, Hq, Hkv, T, D,
@@ -227,3 +240,24 @@ def sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices:
 
 def gate_denominator(proj_dim: int) -> float:
     return float(math.sqrt(proj_dim))
+
+
+def ipc_export(t: torch.Tensor) -> tuple[bytes, int]:
+    """(64-byte CUDA IPC handle of t's allocation, byte offset of t in it)."""
+    _lib.require_cuda(t)
+    h = ctypes.create_string_buffer(64)
+    off = ctypes.c_int64(0)
+    _lib.check(_lib.load().spruce_ipc_export(t.data_ptr(), h, ctypes.byref(off)))
+    return h.raw, off.value
+
+
+def ipc_import(handle: bytes, offset: int) -> tuple[int, int]:
+    """Map a peer allocation into the current device's context: (pointer, mapping base)."""
+    ptr, base = ctypes.c_void_p(), ctypes.c_void_p()
+    buf = ctypes.create_string_buffer(handle, 64)
+    _lib.check(_lib.load().spruce_ipc_import(buf, offset, ctypes.byref(ptr), ctypes.byref(base)))
+    return ptr.value, base.value
+
+
+def ipc_close(base: int) -> None:
+    _lib.check(_lib.load().spruce_ipc_close(base))

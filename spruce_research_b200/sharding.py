@@ -8,6 +8,15 @@ NCCL all-gather reassembles the layer; the later half of a causal row range
 holds ~5% more selected tiles at config 2).  The only exchange is that
 all-gather of the per-rank outputs into the token-major [B, T, Hq, D] tensor
 the next layer's output projection reads.
+
+Two forms of that all-gather:
+* ``fused`` (default): every rank holds a full [B, T, Hq, D] output tensor,
+  the tensors are CUDA-IPC mapped into every other rank, and the attention
+  kernel's epilogue stores each output row into all of them over NVLink
+  while it runs (plain peer stores, no multicast); one tiny NCCL all-reduce
+  afterwards orders the peers' reads after every rank's kernel.
+* ``nccl``: NCCL all_gather_into_tensor of the per-rank chunks plus a
+  permute into the token-major layout.
 """
 from __future__ import annotations
 
@@ -15,6 +24,7 @@ from dataclasses import dataclass
 
 import torch
 
+from . import native
 from .pipeline import SparsePrefillLayer
 
 
@@ -87,3 +97,39 @@ class ShardedSparsePrefill:
         # rank = g * parts + p: [G, parts, B, T/parts, rep, D] -> [B, parts, T/parts, G, rep, D]
         x = gathered.view(kv_heads, s.parts, B, Tc, Hr, D).permute(2, 1, 3, 0, 4, 5)
         return x.reshape(B, tokens, kv_heads * Hr, D)
+
+
+class PeerOutput:
+    """A full output tensor on every rank, mapped into every other rank by CUDA IPC."""
+
+    def __init__(self, shape, dtype, device, group=None):
+        import torch.distributed as dist
+
+        self.local = torch.empty(shape, dtype=dtype, device=device)
+        handle = native.ipc_export(self.local)
+        world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
+        handles = [None] * world
+        dist.all_gather_object(handles, handle, group=group)
+        self._bases = []
+        self.peer_ptrs = []
+        for r, (h, off) in enumerate(handles):
+            if r == rank:
+                continue
+            ptr, base = native.ipc_import(h, off)
+            self.peer_ptrs.append(ptr)
+            self._bases.append(base)
+        self._tick = torch.zeros(1, device=device, dtype=torch.int32)
+        self.group = group
+
+    def fence(self):
+        """Order later reads of ``local`` after every rank's peer stores (stream-ordered)."""
+        import torch.distributed as dist
+
+        dist.all_reduce(self._tick, group=self.group)
+
+    def close(self):
+        for base in self._bases:
+            native.ipc_close(base)
+        self._bases = []
+        self.peer_ptrs = []

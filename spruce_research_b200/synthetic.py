@@ -113,11 +113,14 @@ def make_layer_inputs(shape: LayerShape, dtype: torch.dtype, seed: int, device="
         width = min(plant_blocks, qb)
         top = draw.topk(width, dim=-1)
         chosen = top.indices.masked_fill(top.values < 0, -1)          # [B, Hkv, qb, width]
-        k_add = torch.zeros((B, Hkv, qb + 1, D), device=device, dtype=torch.float32)
-        src = (plant_scale * u)[:, :, :, None, :].expand(B, Hkv, qb, width, D)
-        dst = chosen.masked_fill(chosen < 0, qb)                       # dump slot qb
+        # Accumulated on the CPU: scatter_add_ is sequential (deterministic) there, while the
+        # CUDA version uses atomics whose order, and so rounding, varies between runs and GPUs.
+        k_add = torch.zeros((B, Hkv, qb + 1, D), dtype=torch.float32)
+        src = (plant_scale * u.cpu())[:, :, :, None, :].expand(B, Hkv, qb, width, D)
+        dst = chosen.cpu().masked_fill(chosen.cpu() < 0, qb)           # dump slot qb
         k_add.scatter_add_(2, dst.reshape(B, Hkv, qb * width, 1).expand(B, Hkv, qb * width, D),
                            src.reshape(B, Hkv, qb * width, D))
+        k_add = k_add.to(device)
         q_add = u.repeat_interleave(rep, dim=1)                        # [B, Hq, qb, D]
         q_tok = q_add.repeat_interleave(BLOCK, dim=2)[:, :, :T]        # [B, Hq, T, D]
         k_tok = k_add[:, :, :qb].repeat_interleave(BLOCK, dim=2)[:, :, :T]
