@@ -56,8 +56,14 @@ struct AttnParams {
   int q_begin, nq;  // query blocks [q_begin, q_begin + nq) are computed
   float scale_log2;
   uint32_t* status;
-  void* peer_out[kMaxPeers];  // fused output all-gather targets (NVLink peer memory)
-  int n_peer;
+};
+
+// Output tensor maps: [0] this GPU's output, [1..] the peers' outputs for the
+// fused all-gather (NVLink peer memory, same layout).  Box (64 dims, 1 head,
+// 64 tokens), 128-byte swizzle.
+struct OutMaps {
+  CUtensorMap m[1 + kMaxPeers];
+  int count;
 };
 
 template <int D, int STAGES>
@@ -122,7 +128,8 @@ __device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t (&r)[3
 template <typename T, int D, int STAGES>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
-                          const __grid_constant__ CUtensorMap tmv, const AttnParams p) {
+                          const __grid_constant__ CUtensorMap tmv, const __grid_constant__ OutMaps om,
+                          const AttnParams p) {
   using L = AttnLayout<D, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -422,12 +429,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         ok = __all_sync(0xffffffffu,
                         mbar_wait(&o_done[2 * t + ((n - 1) & 1)], ((n - 1) >> 1) & 1, p.status, abort_flag));
       tc_fence_after();
-      // Epilogue: O / l -> T, row (token, head) of the token-major output.
-      const int hh = 2 * (pair0 + t) + (row & 1);
-      const int token = i * 64 + tok;
-      const bool valid = hh < p.rep && token < p.T;
-      const int64_t orow_off = b * p.osb + (int64_t)(g * p.rep + hh) * p.osh + (int64_t)token * p.ost;
-      T* orow = static_cast<T*>(p.out) + orow_off;
+      // Epilogue: O / l -> T staged in this tile's Q region (every QK MMA is complete
+      // once PV(n-1) is), laid out [panel][head][token][128 B] with the 128-byte
+      // swizzle, then TMA tensor stores to this GPU's output and to each peer's.
+      uint8_t* stage = smem + L::OFF_Q + t * L::Q_TILE;
+      const int hsub = row & 1;
+      const int srow = hsub * 64 + tok;  // staging row: head-major
       const float inv = l > 0.0f ? 1.0f / l : 0.0f;
       if (n == 0 && row == 0) raise_status(p.status, SPRUCE_STATUS_EMPTY_ROW);
 #pragma unroll 1
@@ -440,20 +447,33 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
           for (int e = 0; e < 32; ++e) o[e] = 0.0f;
         }
-        if (valid) {
 #pragma unroll
-          for (int v4 = 0; v4 < 4; ++v4) {
-            uint4 v;
-            v.x = Pack2<T>::pack(o[v4 * 8 + 0] * inv, o[v4 * 8 + 1] * inv);
-            v.y = Pack2<T>::pack(o[v4 * 8 + 2] * inv, o[v4 * 8 + 3] * inv);
-            v.z = Pack2<T>::pack(o[v4 * 8 + 4] * inv, o[v4 * 8 + 5] * inv);
-            v.w = Pack2<T>::pack(o[v4 * 8 + 6] * inv, o[v4 * 8 + 7] * inv);
-            *reinterpret_cast<uint4*>(orow + cc * 32 + v4 * 8) = v;
-            // Fused all-gather: the same row into every peer's output over NVLink.
-            for (int pp = 0; pp < p.n_peer; ++pp)
-              *reinterpret_cast<uint4*>(static_cast<T*>(p.peer_out[pp]) + orow_off + cc * 32 + v4 * 8) = v;
-          }
+        for (int v4 = 0; v4 < 4; ++v4) {
+          uint4 v;
+          v.x = Pack2<T>::pack(o[v4 * 8 + 0] * inv, o[v4 * 8 + 1] * inv);
+          v.y = Pack2<T>::pack(o[v4 * 8 + 2] * inv, o[v4 * 8 + 3] * inv);
+          v.z = Pack2<T>::pack(o[v4 * 8 + 4] * inv, o[v4 * 8 + 5] * inv);
+          v.w = Pack2<T>::pack(o[v4 * 8 + 6] * inv, o[v4 * 8 + 7] * inv);
+          const int col = cc * 32 + v4 * 8;  // first of the 8 dims in this 16-byte chunk
+          const int chunk = (col & 63) >> 3;
+          *reinterpret_cast<uint4*>(stage + (col >> 6) * L::Q_PANEL + srow * 128 + ((chunk ^ (srow & 7)) << 4)) = v;
         }
+      }
+      fence_proxy_async_smem();
+      named_barrier_sync(1 + t, 128);
+      if ((warp & 3) == 0) {
+        if (elect_one()) {
+          for (int dst = 0; dst < om.count; ++dst)
+            for (int h = 0; h < 2; ++h) {
+              const int hh = 2 * (pair0 + t) + h;
+              if (hh >= p.rep) continue;  // the half-filled last tile of an odd group
+              for (int pp = 0; pp < L::NP; ++pp)
+                tma_store_4d(&om.m[dst], stage + pp * L::Q_PANEL + h * 8192, pp * 64, g * p.rep + hh, i * 64, b);
+            }
+          tma_store_commit();
+          tma_store_wait_read();  // shared memory must stay valid until the stores have read it
+        }
+        __syncwarp();
       }
     }
   }
@@ -526,15 +546,19 @@ static cudaError_t launch_typed(const AttnArgs& a, CUtensorMapDataType dt, cudaS
   p.n_cta = (p.n_pair + 1) / 2;
   p.scale_log2 = a.scale * 1.4426950408889634f;
   p.status = a.status;
-  p.n_peer = a.n_peer;
-  for (int pp = 0; pp < kMaxPeers; ++pp) p.peer_out[pp] = pp < a.n_peer ? const_cast<void*>(a.peer_out[pp]) : nullptr;
+  // Output maps over the LOGICAL [B, Hq, T, D] output strides, one head per box.
+  OutMaps om;
+  om.count = 1 + a.n_peer;
+  if (!make_map(&om.m[0], a.out, dt, a.B, a.Hq, a.T, D, a.os, 1)) return cudaErrorInvalidValue;
+  for (int pp = 0; pp < a.n_peer; ++pp)
+    if (!make_map(&om.m[1 + pp], a.peer_out[pp], dt, a.B, a.Hq, a.T, D, a.os, 1)) return cudaErrorInvalidValue;
   const size_t smem = L::smem_bytes(a.Kw);
   auto kern = attn_fwd_sm100_kernel<T, D, STAGES>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   if (p.nq <= 0) return cudaSuccess;
   dim3 grid(p.nq * p.n_cta, a.Hkv, a.B);
-  kern<<<grid, kAttnThreads, smem, stream>>>(tmq, tmk, tmv, p);
+  kern<<<grid, kAttnThreads, smem, stream>>>(tmq, tmk, tmv, om, p);
   return cudaGetLastError();
 }
 
