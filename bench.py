@@ -274,7 +274,7 @@ def run_b200(args):
         """This rank's selector + attention (+ all-gather); q/k/v are its shard's views."""
         if marks is not None:
             marks[0].record()
-        sel = layer.select(qs, ks, out=sel_buf)
+        sel = layer.select(qs, ks, out=sel_buf, q_blocks=(i0, i1))
         if marks is not None:
             marks[1].record()
         native.sparse_attention(qs, ks, vs, sel, out=local_out, q_blocks=(i0, i1), peer_outs=peer_ptrs)

@@ -116,6 +116,16 @@ SPRUCE_API int spruce_gate_select(const float *qp, const float *kp, int64_t B, i
                        int64_t local_window, int64_t sink_blocks, int32_t *out, const int64_t out_strides[3],
                        void *stream);
 
+/*
+ * spruce_gate_select restricted to query blocks [q_block_begin, q_block_end):
+ * only those rows of `out` are written (a GPU that attends a query-block range
+ * of a layer selects just those rows).
+ */
+SPRUCE_API int spruce_gate_select_rows(const float *qp, const float *kp, int64_t B, int64_t G, int64_t qb, int64_t P,
+                                       int64_t K, int64_t local_window, int64_t sink_blocks, int32_t *out,
+                                       const int64_t out_strides[3], int64_t q_block_begin, int64_t q_block_end,
+                                       void *stream);
+
 /* Bytes of workspace spruce_select_blocks needs for this shape. */
 SPRUCE_API int64_t spruce_select_workspace_bytes(int64_t B, int64_t Hkv, int64_t T, int64_t D, int64_t P, int dtype);
 
@@ -130,6 +140,18 @@ SPRUCE_API int spruce_select_blocks(const void *q, const int64_t q_strides[4], c
                          const float *Wk, int64_t P, int64_t K, int64_t local_window, int64_t sink_blocks,
                          int32_t *out, const int64_t out_strides[3], void *workspace, int64_t workspace_bytes,
                          void *stream);
+
+/*
+ * spruce_select_blocks for query blocks [q_block_begin, q_block_end) only:
+ * pools just the query blocks of the range and the key blocks before its end,
+ * projects those rows and selects those rows of `out` (same workspace size).
+ */
+SPRUCE_API int spruce_select_blocks_rows(const void *q, const int64_t q_strides[4], const void *k,
+                                         const int64_t k_strides[4], int dtype, int64_t B, int64_t Hq, int64_t Hkv,
+                                         int64_t T, int64_t D, const float *Wq, const float *Wk, int64_t P, int64_t K,
+                                         int64_t local_window, int64_t sink_blocks, int32_t *out,
+                                         const int64_t out_strides[3], int64_t q_block_begin, int64_t q_block_end,
+                                         void *workspace, int64_t workspace_bytes, void *stream);
 
 /*
  * spruce_select_blocks without a caller workspace; it has no counterpart in

@@ -39,6 +39,9 @@ SIGNATURES = {
     "spruce_gate_project": ([_P, _INT, _I64, _I64, _P, _I64, _P, _P], _INT),
     "spruce_gate_scores": ([_P, _P, _I64, _I64, _I64, _I64, _P, _P], _INT),
     "spruce_gate_select": ([_P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _P], _INT),
+    "spruce_gate_select_rows": ([_P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _I64, _I64, _P], _INT),
+    "spruce_select_blocks_rows": ([_P, _P, _P, _P, _INT, _I64, _I64, _I64, _I64, _I64, _P, _P, _I64, _I64, _I64,
+                                   _I64, _P, _P, _I64, _I64, _P, _I64, _P], _INT),
     "spruce_select_workspace_bytes": ([_I64, _I64, _I64, _I64, _I64, _INT], _I64),
     "spruce_select_blocks": ([_P, _P, _P, _P, _INT, _I64, _I64, _I64, _I64, _I64, _P, _P, _I64, _I64, _I64,
                               _I64, _P, _P, _P, _I64, _P], _INT),

@@ -7,6 +7,7 @@
 // allocates device memory or synchronises.
 #include <cstdarg>
 #include <cstdio>
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -86,6 +87,19 @@ int spruce_group_avg_tokens(const void* x, const int64_t x_strides[4], int dtype
 }
 
 static int pool_jobs(spruce::PoolJob j0, spruce::PoolJob j1, int njobs, int dtype, int64_t B, int64_t T, int64_t D,
+                     void* stream);
+
+// Pooled Q for blocks [q0, q1) and pooled K for blocks [0, k1) (the rows a
+// query-block range of the selector reads); shapes already checked.
+static int pool_qk_range(const void* q, const int64_t q_strides[4], const void* k, const int64_t k_strides[4],
+                         int dtype, int64_t B, int64_t Hq, int64_t Hkv, int64_t T, int64_t D, void* pooled_q,
+                         void* pooled_k, int q0, int q1, int k1, void* stream) {
+  spruce::PoolJob jq{q, q_strides[0], q_strides[1], q_strides[2], pooled_q, (int)(Hq / Hkv), (int)Hkv, q0, q1 - q0};
+  spruce::PoolJob jk{k, k_strides[0], k_strides[1], k_strides[2], pooled_k, 1, (int)Hkv, 0, k1};
+  return pool_jobs(jq, jk, 2, dtype, B, T, D, stream);
+}
+
+static int pool_jobs(spruce::PoolJob j0, spruce::PoolJob j1, int njobs, int dtype, int64_t B, int64_t T, int64_t D,
                      void* stream) {
   cudaError_t e;
   switch (dtype) {
@@ -105,7 +119,8 @@ int spruce_proto_pool(const void* x, const int64_t x_strides[4], int dtype, int6
   if (!aligned16(x) || !aligned16(out) || !vec_strides_ok(x_strides, dtype, D))
     return fail(SPRUCE_ERR_UNSUPPORTED, "x must be 16-byte aligned with a unit last stride");
   if (B == 0 || T == 0) return SPRUCE_OK;
-  spruce::PoolJob j{x, x_strides[0], x_strides[1], x_strides[2], out, 1, (int)H};
+  const int nb = (int)((T + SPRUCE_BLOCK - 1) / SPRUCE_BLOCK);
+  spruce::PoolJob j{x, x_strides[0], x_strides[1], x_strides[2], out, 1, (int)H, 0, nb};
   return pool_jobs(j, j, 1, dtype, B, T, D, stream);
 }
 
@@ -120,9 +135,8 @@ int spruce_pool_qk(const void* q, const int64_t q_strides[4], const void* k, con
       !vec_strides_ok(q_strides, dtype, D) || !vec_strides_ok(k_strides, dtype, D))
     return fail(SPRUCE_ERR_UNSUPPORTED, "q/k must be 16-byte aligned with a unit last stride");
   if (B == 0 || T == 0) return SPRUCE_OK;
-  spruce::PoolJob jq{q, q_strides[0], q_strides[1], q_strides[2], pooled_q, (int)(Hq / Hkv), (int)Hkv};
-  spruce::PoolJob jk{k, k_strides[0], k_strides[1], k_strides[2], pooled_k, 1, (int)Hkv};
-  return pool_jobs(jq, jk, 2, dtype, B, T, D, stream);
+  const int nb = (int)((T + SPRUCE_BLOCK - 1) / SPRUCE_BLOCK);
+  return pool_qk_range(q, q_strides, k, k_strides, dtype, B, Hq, Hkv, T, D, pooled_q, pooled_k, 0, nb, nb, stream);
 }
 
 int spruce_gate_project(const void* x, int dtype, int64_t N, int64_t D, const float* W, int64_t P, float* out,
@@ -155,19 +169,30 @@ static int check_select_policy(int64_t K, int64_t lw, int64_t sink) {
   return SPRUCE_OK;
 }
 
-int spruce_gate_select(const float* qp, const float* kp, int64_t B, int64_t G, int64_t qb, int64_t P, int64_t K,
-                       int64_t local_window, int64_t sink_blocks, int32_t* out, const int64_t out_strides[3],
-                       void* stream) {
+int spruce_gate_select_rows(const float* qp, const float* kp, int64_t B, int64_t G, int64_t qb, int64_t P,
+                            int64_t K, int64_t local_window, int64_t sink_blocks, int32_t* out,
+                            const int64_t out_strides[3], int64_t q_block_begin, int64_t q_block_end, void* stream) {
   int rc = check_select_policy(K, local_window, sink_blocks);
   if (rc) return rc;
   if (B < 0 || G < 1 || qb < 0 || P < 1 || P > 1024) return fail(SPRUCE_ERR_INVALID, "bad selection shape");
-  if (B == 0 || qb == 0) return SPRUCE_OK;
+  if (q_block_begin < 0 || q_block_end > qb || q_block_begin > q_block_end)
+    return fail(SPRUCE_ERR_INVALID, "query-block range [%lld, %lld) outside [0, %lld)", (long long)q_block_begin,
+                (long long)q_block_end, (long long)qb);
+  if (B == 0 || qb == 0 || q_block_begin == q_block_end) return SPRUCE_OK;
   if (spruce::select_rows_for((int)qb, (int)P) == 0)
     return fail(SPRUCE_ERR_UNSUPPORTED, "qb=%lld query blocks exceed the selection kernel's shared memory",
                 (long long)qb);
   return cuda_status(spruce::launch_select(qp, kp, (int)B, (int)G, (int)qb, (int)P, (int)K, (int)local_window,
-                                           (int)sink_blocks, out, out_strides, as_stream(stream)),
+                                           (int)sink_blocks, out, out_strides, (int)q_block_begin,
+                                           (int)q_block_end, as_stream(stream)),
                      "selection launch");
+}
+
+int spruce_gate_select(const float* qp, const float* kp, int64_t B, int64_t G, int64_t qb, int64_t P, int64_t K,
+                       int64_t local_window, int64_t sink_blocks, int32_t* out, const int64_t out_strides[3],
+                       void* stream) {
+  return spruce_gate_select_rows(qp, kp, B, G, qb, P, K, local_window, sink_blocks, out, out_strides, 0,
+                                 qb < 0 ? 0 : qb, stream);
 }
 
 int64_t spruce_select_workspace_bytes(int64_t B, int64_t Hkv, int64_t T, int64_t D, int64_t P, int dtype) {
@@ -182,6 +207,17 @@ int spruce_select_blocks(const void* q, const int64_t q_strides[4], const void* 
                          const float* Wk, int64_t P, int64_t K, int64_t local_window, int64_t sink_blocks,
                          int32_t* out, const int64_t out_strides[3], void* workspace, int64_t workspace_bytes,
                          void* stream) {
+  const int64_t qb = (T + SPRUCE_BLOCK - 1) / SPRUCE_BLOCK;
+  return spruce_select_blocks_rows(q, q_strides, k, k_strides, dtype, B, Hq, Hkv, T, D, Wq, Wk, P, K, local_window,
+                                   sink_blocks, out, out_strides, 0, qb < 0 ? 0 : qb, workspace, workspace_bytes,
+                                   stream);
+}
+
+int spruce_select_blocks_rows(const void* q, const int64_t q_strides[4], const void* k, const int64_t k_strides[4],
+                              int dtype, int64_t B, int64_t Hq, int64_t Hkv, int64_t T, int64_t D, const float* Wq,
+                              const float* Wk, int64_t P, int64_t K, int64_t local_window, int64_t sink_blocks,
+                              int32_t* out, const int64_t out_strides[3], int64_t q_block_begin,
+                              int64_t q_block_end, void* workspace, int64_t workspace_bytes, void* stream) {
   int rc = check_select_policy(K, local_window, sink_blocks);
   if (rc) return rc;
   const int64_t need = spruce_select_workspace_bytes(B, Hkv, T, D, P, dtype);
@@ -197,13 +233,50 @@ int spruce_select_blocks(const void* q, const int64_t q_strides[4], const void* 
   void* pooled_k = ws + up(rows * D * elem_size(dtype));
   float* qp = reinterpret_cast<float*>(ws + 2 * up(rows * D * elem_size(dtype)));
   float* kp = reinterpret_cast<float*>(ws + 2 * up(rows * D * elem_size(dtype)) + up(rows * P * 4));
-  rc = spruce_pool_qk(q, q_strides, k, k_strides, dtype, B, Hq, Hkv, T, D, pooled_q, pooled_k, stream);
+  if (q_block_begin < 0 || q_block_end > qb || q_block_begin > q_block_end)
+    return fail(SPRUCE_ERR_INVALID, "query-block range [%lld, %lld) outside [0, %lld)", (long long)q_block_begin,
+                (long long)q_block_end, (long long)qb);
+  if (!valid_dtype(dtype)) return fail(SPRUCE_ERR_INVALID, "unsupported dtype code %d", dtype);
+  if (B < 0 || Hq < 1 || Hkv < 1 || T < 0 || D < 1 || D > 256 || P < 1 || P > 1024)
+    return fail(SPRUCE_ERR_INVALID, "bad selector shape");
+  if (Hq % Hkv) return fail(SPRUCE_ERR_INVALID, "query heads (%lld) must be divisible by KV heads (%lld)",
+                            (long long)Hq, (long long)Hkv);
+  if (!aligned16(q) || !aligned16(k) || !vec_strides_ok(q_strides, dtype, D) || !vec_strides_ok(k_strides, dtype, D))
+    return fail(SPRUCE_ERR_UNSUPPORTED, "q/k must be 16-byte aligned with a unit last stride");
+  if (B == 0 || T == 0 || q_block_begin == q_block_end) return SPRUCE_OK;
+  // Only the rows the range reads: queries [i0, i1), keys [0, i1 - local_window).
+  const int i0 = (int)q_block_begin, i1 = (int)q_block_end;
+  const int k1 = std::max(1, std::min(i1, (int)qb));
+  rc = pool_qk_range(q, q_strides, k, k_strides, dtype, B, Hq, Hkv, T, D, pooled_q, pooled_k, i0, i1, k1, stream);
   if (rc) return rc;
-  rc = spruce_gate_project(pooled_q, dtype, rows, D, Wq, P, qp, stream);
+  cudaError_t e;
+  switch (dtype) {
+    case SPRUCE_DTYPE_F32:
+      e = spruce::launch_project_rows<float>(pooled_q, B * Hkv, (int)qb, i0, i1 - i0, (int)D, Wq, (int)P, qp,
+                                             as_stream(stream));
+      if (e == cudaSuccess)
+        e = spruce::launch_project_rows<float>(pooled_k, B * Hkv, (int)qb, 0, k1, (int)D, Wk, (int)P, kp,
+                                               as_stream(stream));
+      break;
+    case SPRUCE_DTYPE_BF16:
+      e = spruce::launch_project_rows<__nv_bfloat16>(pooled_q, B * Hkv, (int)qb, i0, i1 - i0, (int)D, Wq, (int)P, qp,
+                                                     as_stream(stream));
+      if (e == cudaSuccess)
+        e = spruce::launch_project_rows<__nv_bfloat16>(pooled_k, B * Hkv, (int)qb, 0, k1, (int)D, Wk, (int)P, kp,
+                                                       as_stream(stream));
+      break;
+    default:
+      e = spruce::launch_project_rows<__half>(pooled_q, B * Hkv, (int)qb, i0, i1 - i0, (int)D, Wq, (int)P, qp,
+                                              as_stream(stream));
+      if (e == cudaSuccess)
+        e = spruce::launch_project_rows<__half>(pooled_k, B * Hkv, (int)qb, 0, k1, (int)D, Wk, (int)P, kp,
+                                                as_stream(stream));
+      break;
+  }
+  rc = cuda_status(e, "projection launch");
   if (rc) return rc;
-  rc = spruce_gate_project(pooled_k, dtype, rows, D, Wk, P, kp, stream);
-  if (rc) return rc;
-  return spruce_gate_select(qp, kp, B, Hkv, qb, P, K, local_window, sink_blocks, out, out_strides, stream);
+  return spruce_gate_select_rows(qp, kp, B, Hkv, qb, P, K, local_window, sink_blocks, out, out_strides, i0, i1,
+                                 stream);
 }
 
 }  // extern "C"

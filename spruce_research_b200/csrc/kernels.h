@@ -12,6 +12,7 @@ struct PoolJob {
   void* out;           // [B, Hout, nb, D] contiguous
   int rep;             // heads averaged per output row (1 = plain pooling)
   int hout;            // output heads
+  int blk0, nblk;      // 64-token blocks [blk0, blk0 + nblk) are pooled
 };
 
 template <typename T>
@@ -21,12 +22,16 @@ cudaError_t launch_group_avg(const void* x, const int64_t* strides, void* out, i
                              int G, cudaStream_t stream);
 template <typename T>
 cudaError_t launch_project(const void* x, int64_t N, int D, const float* W, int P, float* out, cudaStream_t stream);
+// Rows [row0, row0 + nrows) of each of `groups` consecutive [qb, D] matrices.
+template <typename T>
+cudaError_t launch_project_rows(const void* x, int64_t groups, int qb, int row0, int nrows, int D, const float* W,
+                                int P, float* out, cudaStream_t stream);
 
 cudaError_t launch_scores(const float* qp, const float* kp, int64_t R, int qb, int kb, int P, float* out,
                           cudaStream_t stream);
 int select_rows_for(int qb, int P);
 cudaError_t launch_select(const float* qp, const float* kp, int B, int G, int qb, int P, int K, int lw, int sink,
-                          int32_t* out, const int64_t* out_strides, cudaStream_t stream);
+                          int32_t* out, const int64_t* out_strides, int q_begin, int q_end, cudaStream_t stream);
 cudaError_t launch_pack_ids(const int64_t* ids, int64_t R, int qb, int C, int K, int lw, int kb, int sink,
                             int32_t* out, cudaStream_t stream);
 cudaError_t launch_validate(const int32_t* sel, int64_t rows, int qb, int K, int lw, int64_t* result,

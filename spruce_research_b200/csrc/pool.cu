@@ -42,10 +42,11 @@ __global__ void __launch_bounds__(kPoolThreads) pool_block_kernel(PoolJob j0, Po
   float* rows = pool_smem;                 // [64][D] group-averaged, already rounded to T
   float* part = pool_smem + kPoolBlock * D; // [4][D] 16-row partial sums
 
-  const int i = blockIdx.x;
   int y = blockIdx.y;
   const PoolJob& job = (njobs > 1 && y >= j0.hout) ? j1 : j0;
   if (njobs > 1 && y >= j0.hout) y -= j0.hout;
+  if (static_cast<int>(blockIdx.x) >= job.nblk) return;
+  const int i = job.blk0 + blockIdx.x;
   const int b = blockIdx.z;
   const int t0 = i * kPoolBlock;
   const int count = min(kPoolBlock, T_len - t0);
@@ -140,7 +141,9 @@ cudaError_t launch_pool(PoolJob j0, PoolJob j1, int njobs, int B, int T_len, int
                                          (int)smem);
     if (e != cudaSuccess) return e;
   }
-  dim3 grid(nb, j0.hout + (njobs > 1 ? j1.hout : 0), B);
+  const int gx = njobs > 1 ? std::max(j0.nblk, j1.nblk) : j0.nblk;
+  if (gx <= 0) return cudaSuccess;
+  dim3 grid(gx, j0.hout + (njobs > 1 ? j1.hout : 0), B);
   pool_block_kernel<T><<<grid, kPoolThreads, smem, stream>>>(j0, j1, njobs, T_len, D, nb);
   return cudaGetLastError();
 }

@@ -21,13 +21,16 @@ namespace spruce {
 // ------------------------------------------------------------------ projection
 constexpr int kProjRows = 8;
 
+// Row n of the launch is row (n / nrows) * qb + row0 + n % nrows of x (and of out).
 template <typename T>
 __global__ void __launch_bounds__(128) project_kernel(const T* __restrict__ x, int64_t N, int D,
-                                                      const float* __restrict__ W, int P, float* __restrict__ out) {
+                                                      const float* __restrict__ W, int P, float* __restrict__ out,
+                                                      int qb, int row0, int nrows) {
   extern __shared__ float xs[];  // [kProjRows][D]
   const int64_t n0 = (int64_t)blockIdx.x * kProjRows;
   const int rows = (int)(N - n0 < kProjRows ? N - n0 : kProjRows);
-  for (int e = threadIdx.x; e < rows * D; e += blockDim.x) xs[e] = Elem<T>::to_f(x[n0 * D + e]);
+  auto map_row = [&](int64_t n) { return (n / nrows) * qb + row0 + n % nrows; };
+  for (int e = threadIdx.x; e < rows * D; e += blockDim.x) xs[e] = Elem<T>::to_f(x[map_row(n0 + e / D) * D + e % D]);
   __syncthreads();
   for (int p = threadIdx.x; p < P; p += blockDim.x) {
     float acc[kProjRows];
@@ -38,7 +41,7 @@ __global__ void __launch_bounds__(128) project_kernel(const T* __restrict__ x, i
 #pragma unroll
       for (int r = 0; r < kProjRows; ++r) acc[r] = __fmaf_rn(xs[r * D + d], w, acc[r]);
     }
-    for (int r = 0; r < rows; ++r) out[(n0 + r) * P + p] = acc[r];
+    for (int r = 0; r < rows; ++r) out[map_row(n0 + r) * P + p] = acc[r];
   }
 }
 
@@ -59,7 +62,8 @@ __device__ __forceinline__ uint32_t order_key(float f) {
 // Writes fp32 scores of columns [j0, j0 + 256) ∩ [0, ncols) via `emit(r, j, s)`.
 template <int ROWS, typename Emit>
 __device__ __forceinline__ void score_columns(const float* qs, const float* __restrict__ kp, int P, int j0,
-                                              int ncols, float* kT, float denom, Emit emit) {
+                                              int ncols, float* kT, float denom, Emit emit, int qstride = -1) {
+  if (qstride < 0) qstride = P;
   const int t = threadIdx.x;
   float acc[ROWS];
 #pragma unroll
@@ -78,7 +82,7 @@ __device__ __forceinline__ void score_columns(const float* qs, const float* __re
     for (int pp = 0; pp < pn; ++pp) {
       const float kv = kT[pp * kScoreThreads + t];
 #pragma unroll
-      for (int r = 0; r < ROWS; ++r) acc[r] = __fmaf_rn(qs[r * P + p0 + pp], kv, acc[r]);
+      for (int r = 0; r < ROWS; ++r) acc[r] = __fmaf_rn(qs[r * qstride + p0 + pp], kv, acc[r]);
     }
   }
   const int j = j0 + t;
@@ -88,24 +92,89 @@ __device__ __forceinline__ void score_columns(const float* qs, const float* __re
   }
 }
 
+// 16 query rows x 256 key columns with 4x4 register micro-tiles: thread t owns
+// rows 4*(t/64)..+3 and columns j0 + (t%64) + 64*c, c = 0..3.  Key
+// projections are staged 32 p at a time, row-major with a 36-float stride
+// (conflict-free 16-byte loads); query rows are read as broadcast float4s.
+// Every output is still one fma chain over p = 0..P-1 in order, so scores
+// equal score_columns' (and the CPU restatement's) bit for bit.
+constexpr int kKStride = 36;
+
+template <typename Emit>
+__device__ __forceinline__ void score_tile16(const float* qs, int qstride, const float* __restrict__ kp, int P,
+                                             int j0, int ncols, float* ks, float denom, Emit emit) {
+  const int t = threadIdx.x;
+  const int rg = t >> 6;
+  const int cg = t & 63;
+  float acc[4][4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) acc[r][c] = 0.0f;
+  for (int p0 = 0; p0 < P; p0 += kPChunk) {
+    const int pn = min(kPChunk, P - p0);
+    __syncthreads();
+    for (int e = t; e < kScoreThreads * kPChunk; e += kScoreThreads) {
+      const int jj = e >> 5;
+      const int pp = e & 31;
+      const int j = j0 + jj;
+      ks[jj * kKStride + pp] = (j < ncols && pp < pn) ? __ldg(kp + (int64_t)j * P + p0 + pp) : 0.0f;
+    }
+    __syncthreads();
+    int pp = 0;
+    for (; pp + 4 <= pn; pp += 4) {
+      float4 qv[4], kv[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) qv[r] = *reinterpret_cast<const float4*>(qs + (4 * rg + r) * qstride + p0 + pp);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) kv[c] = *reinterpret_cast<const float4*>(ks + (cg + 64 * c) * kKStride + pp);
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          acc[r][c] = __fmaf_rn(qv[r].x, kv[c].x, acc[r][c]);
+          acc[r][c] = __fmaf_rn(qv[r].y, kv[c].y, acc[r][c]);
+          acc[r][c] = __fmaf_rn(qv[r].z, kv[c].z, acc[r][c]);
+          acc[r][c] = __fmaf_rn(qv[r].w, kv[c].w, acc[r][c]);
+        }
+    }
+    for (; pp < pn; ++pp)
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          acc[r][c] = __fmaf_rn(qs[(4 * rg + r) * qstride + p0 + pp], ks[(cg + 64 * c) * kKStride + pp], acc[r][c]);
+  }
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const int j = j0 + cg + 64 * c;
+    if (j < ncols)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) emit(4 * rg + r, j, __fdiv_rn(acc[r][c], denom));
+  }
+}
+
 // Full score matrix (FlatGate.forward, P = 1): grid (ceil(qb/ROWS), R).
 template <int ROWS>
 __global__ void __launch_bounds__(kScoreThreads) scores_kernel(const float* __restrict__ qp,
                                                                const float* __restrict__ kp, int qb, int kb, int P,
                                                                float* __restrict__ out, float denom) {
+  static_assert(ROWS == 16, "the full-matrix scorer uses 16-row tiles");
   extern __shared__ float sm[];
-  float* qs = sm;                   // [ROWS][P]
-  float* kT = sm + ROWS * P;        // [kPChunk][256]
+  const int qstride = (P + 3) / 4 * 4 + 4;
+  float* qs = sm;                   // [16][qstride]
+  float* kT = sm + ROWS * qstride;  // [256][kKStride]
   const int r0 = blockIdx.x * ROWS;
   const int64_t mat = blockIdx.y;
   const float* q = qp + mat * qb * P;
   const float* k = kp + mat * kb * P;
-  for (int e = threadIdx.x; e < ROWS * P; e += kScoreThreads) {
-    const int r = e / P;
-    qs[e] = (r0 + r < qb) ? q[(int64_t)(r0 + r) * P + e % P] : 0.0f;
+  for (int e = threadIdx.x; e < ROWS * qstride; e += kScoreThreads) {
+    const int r = e / qstride;
+    const int pcol = e % qstride;
+    qs[e] = (r0 + r < qb && pcol < P) ? q[(int64_t)(r0 + r) * P + pcol] : 0.0f;
   }
   for (int j0 = 0; j0 < kb; j0 += kScoreThreads) {
-    score_columns<ROWS>(qs, k, P, j0, kb, kT, denom, [&](int r, int j, float s) {
+    score_tile16(qs, qstride, k, P, j0, kb, kT, denom, [&](int r, int j, float s) {
       if (r0 + r < qb) out[(mat * qb + r0 + r) * kb + j] = s;
     });
   }
@@ -116,6 +185,7 @@ struct SelectArgs {
   const float* qp;   // [B, G, qb, P]
   const float* kp;   // [B, G, qb, P]
   int B, G, qb, P, K, local_window, sink, W;
+  int q_begin, q_end;  // query-block rows [q_begin, q_end) are selected
   int32_t* out;
   int64_t osb, osg, osq;
   float denom;
@@ -173,34 +243,41 @@ __global__ void __launch_bounds__(kScoreThreads) select_kernel(SelectArgs a) {
   extern __shared__ float sm[];
   const int P = a.P;
   const int qb = a.qb;
-  float* qs = sm;                                   // [ROWS][P]
-  float* kT = qs + ROWS * P;                        // [kPChunk][256]
-  int* hist = reinterpret_cast<int*>(kT + kPChunk * kScoreThreads);  // [8 warps][256]
+  const int qstride = (P + 3) / 4 * 4 + 4;           // padded row stride of qs (16-byte aligned rows)
+  float* qs = sm;                                   // [ROWS][qstride]
+  float* kT = qs + ROWS * qstride;                  // staging: [256][kKStride] or [kPChunk][256]
+  int* hist = reinterpret_cast<int*>(kT + kScoreThreads * kKStride);  // [8 warps][256]
   uint32_t* keys = reinterpret_cast<uint32_t*>(hist + 8 * 256);     // [ROWS][qb]
 
-  const int tiles = (qb + ROWS - 1) / ROWS;
+  const int tiles = (a.q_end - a.q_begin + ROWS - 1) / ROWS;
   const int tile = tiles - 1 - blockIdx.x;          // heavy (late) rows first
   const int g = blockIdx.y, b = blockIdx.z;
-  const int r0 = tile * ROWS;
+  const int r0 = a.q_begin + tile * ROWS;
   const int64_t mat = (int64_t)b * a.G + g;
   const float* q = a.qp + mat * qb * P;
   const float* k = a.kp + mat * qb * P;
-  for (int e = threadIdx.x; e < ROWS * P; e += kScoreThreads) {
-    const int r = e / P;
-    qs[e] = (r0 + r < qb) ? q[(int64_t)(r0 + r) * P + e % P] : 0.0f;
+  for (int e = threadIdx.x; e < ROWS * qstride; e += kScoreThreads) {
+    const int r = e / qstride;
+    const int pcol = e % qstride;
+    qs[e] = (r0 + r < a.q_end && pcol < P) ? q[(int64_t)(r0 + r) * P + pcol] : 0.0f;
   }
   // Only candidates j < q - local_window of the tile's last row are needed.
   const int ncols = max(0, min(qb, r0 + ROWS - a.local_window));
   for (int j0 = 0; j0 < ncols; j0 += kScoreThreads) {
-    score_columns<ROWS>(qs, k, P, j0, ncols, kT, a.denom,
-                        [&](int r, int j, float s) { keys[r * qb + j] = order_key(s); });
+    if constexpr (ROWS == 16) {
+      score_tile16(qs, qstride, k, P, j0, ncols, kT, a.denom,
+                   [&](int r, int j, float s) { keys[r * qb + j] = order_key(s); });
+    } else {
+      score_columns<ROWS>(qs, k, P, j0, ncols, kT, a.denom,
+                          [&](int r, int j, float s) { keys[r * qb + j] = order_key(s); }, qstride);
+    }
   }
   __syncthreads();
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int r = warp; r < ROWS; r += kScoreThreads / 32) {
     const int i = r0 + r;
-    if (i >= qb) break;
+    if (i >= a.q_end) break;
     const uint32_t* kr = keys + r * qb;
     const int lo = a.sink;
     const int hi = min(qb, i - a.local_window);
@@ -382,9 +459,26 @@ cudaError_t launch_project(const void* x, int64_t N, int D, const float* W, int 
   if (N == 0) return cudaSuccess;
   const int grid = (int)((N + kProjRows - 1) / kProjRows);
   const size_t smem = sizeof(float) * kProjRows * D;
-  project_kernel<T><<<grid, 128, smem, stream>>>(static_cast<const T*>(x), N, D, W, P, out);
+  project_kernel<T><<<grid, 128, smem, stream>>>(static_cast<const T*>(x), N, D, W, P, out, (int)N, 0, (int)N);
   return cudaGetLastError();
 }
+
+template <typename T>
+cudaError_t launch_project_rows(const void* x, int64_t groups, int qb, int row0, int nrows, int D, const float* W,
+                                int P, float* out, cudaStream_t stream) {
+  const int64_t N = groups * nrows;
+  if (N == 0) return cudaSuccess;
+  const int grid = (int)((N + kProjRows - 1) / kProjRows);
+  const size_t smem = sizeof(float) * kProjRows * D;
+  project_kernel<T><<<grid, 128, smem, stream>>>(static_cast<const T*>(x), N, D, W, P, out, qb, row0, nrows);
+  return cudaGetLastError();
+}
+template cudaError_t launch_project_rows<float>(const void*, int64_t, int, int, int, int, const float*, int, float*,
+                                                cudaStream_t);
+template cudaError_t launch_project_rows<__nv_bfloat16>(const void*, int64_t, int, int, int, int, const float*, int,
+                                                        float*, cudaStream_t);
+template cudaError_t launch_project_rows<__half>(const void*, int64_t, int, int, int, int, const float*, int, float*,
+                                                 cudaStream_t);
 template cudaError_t launch_project<float>(const void*, int64_t, int, const float*, int, float*, cudaStream_t);
 template cudaError_t launch_project<__nv_bfloat16>(const void*, int64_t, int, const float*, int, float*,
                                                    cudaStream_t);
@@ -395,7 +489,7 @@ static float gate_denom(int P) { return static_cast<float>(std::sqrt(static_cast
 cudaError_t launch_scores(const float* qp, const float* kp, int64_t R, int qb, int kb, int P, float* out,
                           cudaStream_t stream) {
   constexpr int ROWS = 16;
-  const size_t smem = sizeof(float) * (ROWS * P + kPChunk * kScoreThreads);
+  const size_t smem = sizeof(float) * (ROWS * ((P + 3) / 4 * 4 + 4) + kScoreThreads * kKStride);
   cudaError_t e = cudaFuncSetAttribute(scores_kernel<ROWS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   dim3 grid((qb + ROWS - 1) / ROWS, (unsigned)R);
@@ -404,7 +498,8 @@ cudaError_t launch_scores(const float* qp, const float* kp, int64_t R, int qb, i
 }
 
 size_t select_smem_bytes(int rows, int qb, int P) {
-  return sizeof(float) * (rows * P + kPChunk * kScoreThreads) + sizeof(int) * 8 * 256 +
+  const int qstride = (P + 3) / 4 * 4 + 4;
+  return sizeof(float) * (rows * qstride + kScoreThreads * kKStride) + sizeof(int) * 8 * 256 +
          sizeof(uint32_t) * (size_t)rows * qb;
 }
 
@@ -413,7 +508,8 @@ static cudaError_t launch_select_rows(const SelectArgs& a, cudaStream_t stream) 
   const size_t smem = select_smem_bytes(ROWS, a.qb, a.P);
   cudaError_t e = cudaFuncSetAttribute(select_kernel<ROWS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  dim3 grid((a.qb + ROWS - 1) / ROWS, a.G, a.B);
+  if (a.q_end <= a.q_begin) return cudaSuccess;
+  dim3 grid((a.q_end - a.q_begin + ROWS - 1) / ROWS, a.G, a.B);
   select_kernel<ROWS><<<grid, kScoreThreads, smem, stream>>>(a);
   return cudaGetLastError();
 }
@@ -427,8 +523,10 @@ int select_rows_for(int qb, int P) {
 }
 
 cudaError_t launch_select(const float* qp, const float* kp, int B, int G, int qb, int P, int K, int lw, int sink,
-                          int32_t* out, const int64_t* out_strides, cudaStream_t stream) {
+                          int32_t* out, const int64_t* out_strides, int q_begin, int q_end, cudaStream_t stream) {
   SelectArgs a;
+  a.q_begin = q_begin;
+  a.q_end = q_end;
   a.qp = qp;
   a.kp = kp;
   a.B = B;

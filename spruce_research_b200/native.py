@@ -135,8 +135,12 @@ def select_workspace_bytes(q: torch.Tensor, k: torch.Tensor, proj_dim: int) -> i
 
 def select_blocks(q: torch.Tensor, k: torch.Tensor, Wq: torch.Tensor, Wk: torch.Tensor, k_selected: int,
                   local_window: int = 0, sink_blocks: int = 1, out: torch.Tensor | None = None,
-                  workspace: torch.Tensor | None = None) -> torch.Tensor:
-    """Whole flat selector of one layer: int32 rows [B, Hkv, qb, K] (or into `out`)."""
+                  workspace: torch.Tensor | None = None, q_blocks: tuple[int, int] | None = None) -> torch.Tensor:
+    """Whole flat selector of one layer: int32 rows [B, Hkv, qb, K] (or into `out`).
+
+    With ``q_blocks=(i0, i1)`` only rows i0..i1-1 are selected (and only the
+    blocks they read are pooled and projected).
+    """
     _lib.require_cuda(q, k, Wq, Wk)
     B, Hq, T, d = q.shape
     Hkv = k.shape[1]
@@ -155,12 +159,13 @@ def select_blocks(q: torch.Tensor, k: torch.Tensor, Wq: torch.Tensor, Wk: torch.
     need = select_workspace_bytes(q, k, p)
     if workspace is None or workspace.numel() * workspace.element_size() < need:
         workspace = torch.empty(max(need, 16), device=q.device, dtype=torch.uint8)
+    i0, i1 = (0, qb) if q_blocks is None else q_blocks
     L = _lib.load()
-    _lib.check(L.spruce_select_blocks(q.data_ptr(), _lib.strides(q), k.data_ptr(), _lib.strides(k), _dt(q), B, Hq,
-                                      Hkv, T, d, Wq.data_ptr(), Wk.data_ptr(), p, k_selected, local_window,
-                                      sink_blocks, out.data_ptr(), _lib.int64s(*out.stride()[:3]),
-                                      workspace.data_ptr(), workspace.numel() * workspace.element_size(),
-                                      _lib.stream_of(q)))
+    _lib.check(L.spruce_select_blocks_rows(q.data_ptr(), _lib.strides(q), k.data_ptr(), _lib.strides(k), _dt(q), B,
+                                           Hq, Hkv, T, d, Wq.data_ptr(), Wk.data_ptr(), p, k_selected, local_window,
+                                           sink_blocks, out.data_ptr(), _lib.int64s(*out.stride()[:3]), i0, i1,
+                                           workspace.data_ptr(), workspace.numel() * workspace.element_size(),
+                                           _lib.stream_of(q)))
     return out
 
 

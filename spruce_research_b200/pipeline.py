@@ -38,16 +38,17 @@ class SparsePrefillLayer:
         self.sink_blocks = int(sink_blocks)
         self._workspace = None
 
-    def select(self, q: torch.Tensor, k: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    def select(self, q: torch.Tensor, k: torch.Tensor, out: torch.Tensor | None = None,
+               q_blocks: tuple[int, int] | None = None) -> torch.Tensor:
         need = native.select_workspace_bytes(q, k, self.wq.shape[1])
         if self._workspace is None or self._workspace.numel() < need or self._workspace.device != q.device:
             self._workspace = torch.empty(max(need, 16), device=q.device, dtype=torch.uint8)
         return native.select_blocks(q, k, self.wq, self.wk, self.k_selected, self.local_window,
-                                    self.sink_blocks, out=out, workspace=self._workspace)
+                                    self.sink_blocks, out=out, workspace=self._workspace, q_blocks=q_blocks)
 
     def __call__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor | None = None,
                  selected: torch.Tensor | None = None, q_blocks: tuple[int, int] | None = None):
-        selected = self.select(q, k, out=selected)
+        selected = self.select(q, k, out=selected, q_blocks=q_blocks)
         out = native.sparse_attention(q, k, v, selected, out=out, q_blocks=q_blocks)
         return out, selected
 

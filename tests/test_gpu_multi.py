@@ -52,7 +52,8 @@ def _rank(rank, world, port, q_blocks_tokens, errors):
         dist.barrier(device_ids=[rank])
         view = peer.local[:, :, g0 * rep:g1 * rep]
         ptrs = [p + view.storage_offset() * view.element_size() for p in peer.peer_ptrs]
-        sel = layer.select(q[:, g0 * rep:g1 * rep], k[:, g0:g1])
+        i0, i1 = s.q_blocks
+        sel = layer.select(q[:, g0 * rep:g1 * rep], k[:, g0:g1], q_blocks=(i0, i1))
         native.sparse_attention(q[:, g0 * rep:g1 * rep], k[:, g0:g1], v[:, g0:g1], sel, out=view,
                                 q_blocks=s.q_blocks, peer_outs=ptrs)
         peer.fence()
@@ -67,7 +68,7 @@ def _rank(rank, world, port, q_blocks_tokens, errors):
                        f"{torch.equal(mine, ref[:, i0 * 64:i1 * 64, own])}; zeros left="
                        f"{(peer.local == 0).float().mean().item():.4f}; "
                        f"max abs diff {(peer.local.float() - ref.float()).abs().max().item():.3e}")
-        if not torch.equal(sel, sel_full[:, g0:g1]):
+        if not torch.equal(sel[:, :, i0:i1], sel_full[:, g0:g1, i0:i1]):
             errors.put(f"rank {rank}: sharded selection differs")
     except Exception as e:
         errors.put(f"rank {rank}: {type(e).__name__}: {e}")
