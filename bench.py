@@ -51,6 +51,7 @@ def parse_args():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-chunks", type=int, default=16, help="query-block chunks of the streamed e2e step")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target length of one CPU sample")
     ap.add_argument("--gather", choices=("fused", "nccl"), default="fused",
                     help="N>1 output all-gather: NVLink peer stores in the attention epilogue, or NCCL")
@@ -229,7 +230,7 @@ def run_b200(args):
     import torch.distributed as dist
 
     from spruce_research_b200 import native
-    from spruce_research_b200.pipeline import SparsePrefillLayer
+    from spruce_research_b200.pipeline import HostStreamedLayer, SparsePrefillLayer
     from spruce_research_b200.sharding import PeerOutput, ShardedSparsePrefill, plan
     from spruce_research_b200.synthetic import make_gate_weights, make_layer_inputs
 
@@ -332,14 +333,22 @@ def run_b200(args):
         hv = v[:, g0:g1].transpose(1, 2).contiguous().cpu().pin_memory()
         dq, dk, dv = (torch.empty_like(t, device=dev) for t in (hq, hk, hv))
         hout = torch.empty((B, T, shape.q_heads, D), dtype=torch.bfloat16).pin_memory() if rank == 0 else None
+        streamer = HostStreamedLayer(layer, dev, chunks=args.e2e_chunks)
 
         def e2e_step():
-            dq.copy_(hq, non_blocking=True)
-            dk.copy_(hk, non_blocking=True)
-            dv.copy_(hv, non_blocking=True)
-            out = step(dq.transpose(1, 2), dk.transpose(1, 2), dv.transpose(1, 2))
+            # H2D of chunk c+1, selector + attention of chunk c and D2H of chunk c-1 overlap
+            if world == 1:
+                streamer(hq, hk, hv, dq, dk, dv, local_out, hout=hout, q_blocks=(i0, i1))
+                return
+            streamer(hq, hk, hv, dq, dk, dv, local_out, q_blocks=(i0, i1), peer_outs=peer_ptrs)
+            full = local_out
+            if fused:
+                peer.fence()
+                full = peer.local
+            else:
+                full = runner.gather(local_out[:, i0 * 64:i1 * 64], shape.kv_heads, T)
             if rank == 0:
-                hout.copy_(out, non_blocking=True)
+                hout.copy_(full, non_blocking=True)
 
         for _ in range(max(1, args.warmup)):
             e2e_step()
@@ -354,7 +363,9 @@ def run_b200(args):
         e2e = {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
                "h2d_bytes_per_step": int(sum(t.numel() * t.element_size() for t in (hq, hk, hv))),
                "d2h_bytes_per_step": int(hout.numel() * hout.element_size()) if rank == 0 else 0,
-               "path": "pinned host Q/K/V -> SparsePrefillLayer (selector + attention) -> pinned host output"}
+               "path": ("pinned host Q/K/V -> HostStreamedLayer (copies of chunk c+1, selector + attention of "
+                        f"chunk c and copy-back of chunk c-1 overlap; {args.e2e_chunks} query-block chunks) -> "
+                        "pinned host output")}
         del dq, dk, dv
 
     # ---- CPU baseline (rank 0, single GPU only)

@@ -56,3 +56,75 @@ class SparsePrefillLayer:
 def sparse_prefill_layer(q, k, v, wq, wk, k_selected, local_window=0, sink_blocks=1):
     """Functional form of :class:`SparsePrefillLayer` (allocates its buffers)."""
     return SparsePrefillLayer(wq, wk, k_selected, local_window, sink_blocks)(q, k, v)
+
+
+class HostStreamedLayer:
+    """One layer fed from pinned host buffers, pipelined over query-block chunks.
+
+    Chunk c covers query blocks [i0, i1).  Causality means its selection and
+    attention read only K/V blocks < i1, i.e. chunks 0..c, so three streams
+    overlap the host->device copy of chunk c+1, the selector + attention of
+    chunk c and the device->host copy of chunk c-1.  The PCIe copies, not
+    the kernels, bound a layer fed from the host (1.2 GB in, 0.94 GB out per
+    128K layer), and here they overlap each other and the compute.
+
+    ``after_attention(i0, i1)`` runs on the compute stream after each
+    chunk's attention (the multi-GPU fence of the fused output all-gather).
+    """
+
+    def __init__(self, layer: SparsePrefillLayer, device, chunks: int = 8):
+        self.layer = layer
+        self.chunks = chunks
+        self.h2d = torch.cuda.Stream(device)
+        self.compute = torch.cuda.Stream(device)
+        self.d2h = torch.cuda.Stream(device)
+        self._sel = None
+
+    def __call__(self, hq, hk, hv, dq, dk, dv, dout, hout=None, q_blocks=None, peer_outs=None,
+                 after_attention=None, copy_out=True):
+        """hq/hk/hv pinned token-major [B, T, H, D]; dq/dk/dv/dout device tensors of the same shapes.
+
+        ``dout`` receives the layer output ([B, T, Hq, D]); with ``hout`` and
+        ``copy_out`` it is streamed back to the host chunk by chunk.
+        """
+        B, T, Hq, D = hq.shape
+        Hkv = hk.shape[2]
+        qb = (T + BLOCK - 1) // BLOCK
+        r0, r1 = (0, qb) if q_blocks is None else q_blocks
+        C = max(1, min(self.chunks, r1 - r0))
+        bounds = [r0 + (r1 - r0) * c // C for c in range(C + 1)]
+        dev = dq.device
+        if self._sel is None or self._sel.shape != (B, Hkv, qb, self.layer.k_selected) or self._sel.device != dev:
+            self._sel = torch.empty((B, Hkv, qb, self.layer.k_selected), device=dev, dtype=torch.int32)
+        cur = torch.cuda.current_stream(dev)
+        for s in (self.h2d, self.compute, self.d2h):
+            s.wait_stream(cur)
+        qv, kv, vv = dq.transpose(1, 2), dk.transpose(1, 2), dv.transpose(1, 2)
+        loaded = 0  # tokens already on the device (K/V rows of earlier chunks stay resident)
+        for c in range(C):
+            i0, i1 = bounds[c], bounds[c + 1]
+            t1 = min(i1 * BLOCK, T)
+            h_done = torch.cuda.Event()
+            with torch.cuda.stream(self.h2d):
+                # everything up to this chunk's last token: its queries, and keys/values it may attend
+                dq[:, loaded:t1].copy_(hq[:, loaded:t1], non_blocking=True)
+                dk[:, loaded:t1].copy_(hk[:, loaded:t1], non_blocking=True)
+                dv[:, loaded:t1].copy_(hv[:, loaded:t1], non_blocking=True)
+                h_done.record()
+            loaded = t1
+            c_done = torch.cuda.Event()
+            with torch.cuda.stream(self.compute):
+                self.compute.wait_event(h_done)
+                sel = self.layer.select(qv, kv, out=self._sel, q_blocks=(i0, i1))
+                native.sparse_attention(qv, kv, vv, sel, out=dout, q_blocks=(i0, i1), peer_outs=peer_outs)
+                if after_attention is not None:
+                    after_attention(i0, i1)
+                c_done.record()
+            if hout is not None and copy_out:
+                with torch.cuda.stream(self.d2h):
+                    self.d2h.wait_event(c_done)
+                    t0 = i0 * BLOCK
+                    hout[:, t0:t1].copy_(dout[:, t0:t1], non_blocking=True)
+        for s in (self.h2d, self.compute, self.d2h):
+            cur.wait_stream(s)
+        return dout

@@ -1,0 +1,35 @@
+"""The per-layer pipeline: SparsePrefillLayer and the host-streamed chunked form.
+
+The streamed layer overlaps host copies with the selector and attention of
+earlier query-block chunks; its output must equal the one-shot layer bit for
+bit, including selections that depend on keys copied in earlier chunks.
+"""
+import pytest
+import torch
+
+from oracle import oracle as O
+from spruce_research_b200.pipeline import HostStreamedLayer, SparsePrefillLayer
+from spruce_research_b200.synthetic import LayerShape, k_for_density, make_gate_weights, make_layer_inputs
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("tokens,chunks", [(8192, 4), (8192 + 100, 3), (2048, 8)])
+def test_streamed_layer_equals_one_shot_layer(tokens, chunks):
+    shape = LayerShape(1, 28, 4, tokens, 128)
+    K = k_for_density(shape.query_blocks, 0.10)
+    q, k, v = make_layer_inputs(shape, torch.bfloat16, seed=21)
+    wq, wk = make_gate_weights(1, 128, 128, seed=22)
+    layer = SparsePrefillLayer(wq[0].cuda(), wk[0].cuda(), K)
+    hq, hk, hv = (t.transpose(1, 2).contiguous().pin_memory() for t in (q, k, v))   # token-major host buffers
+    want, sel = layer(*(t.cuda().transpose(1, 2) for t in (hq, hk, hv)))
+    dq, dk, dv = (torch.empty_like(t, device="cuda") for t in (hq, hk, hv))
+    dout = torch.empty_like(want)
+    hout = torch.empty(want.shape, dtype=want.dtype).pin_memory()
+    HostStreamedLayer(layer, torch.device("cuda"), chunks=chunks)(hq, hk, hv, dq, dk, dv, dout, hout=hout)
+    torch.cuda.synchronize()
+    assert torch.equal(dout, want)
+    assert torch.equal(hout, want.cpu())
+    # and the one-shot layer against the oracle's selector
+    ref = O.select_blocks(q, k, wq[0], wk[0], K, 0, 1)
+    assert torch.equal(sel.cpu(), ref["selected"])
