@@ -393,7 +393,7 @@ def run_b200(args):
         "config": config_dict(args, shape, K, entries, world),
         "breakdown_ms": {"selector": sel_ms_max, "attention": attn_ms_max,
                          ("fence" if fused else "gather"): gather_ms_max},
-        "roofline": {"bound": "tensor", "kernel": "attn_fwd_sm100_kernel<bf16,128,3>",
+        "roofline": {"bound": "tensor", "kernel": "attn_fwd_sm100_kernel<bf16,128,4>",
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                      "peak_source": peak_src + ", of measured",
                      "flops_per_launch": r_flops, "traffic": profiled_traffic(shape.tokens)},

@@ -268,6 +268,31 @@ SPRUCE_API int spruce_ipc_export(const void *ptr, void *handle, int64_t *offset)
 SPRUCE_API int spruce_ipc_import(const void *handle, int64_t offset, void **ptr, void **base);
 SPRUCE_API int spruce_ipc_close(void *base);
 
+/*
+ * build_kv_summary_table, sparse/summaries.py:52-142 (token ranges of
+ * _prototype_token_ranges :29-49): for every node n of a residual tree
+ * (block ranges node_starts/node_ends, ResidualTreeLayout.starts/ends of
+ * interfaces/residual_summaries.py:20-71) and prototype p < prototypes, the
+ * mean of the valid K and V rows in token range
+ *   [ts + len*p/P, ts + len*(p+1)/P),  ts/te = start/end * block_size clamped to T,
+ * taken as the difference of fp32 prefix sums and divided by max(count, 1),
+ * as the reference does.  key/value [B, Hkv, T, D] (unit last stride, equal
+ * shapes), valid uint8 [B, T] contiguous or NULL (all tokens valid).
+ * Outputs (contiguous fp32): keys/values [B, Hkv, nodes, P, D],
+ * counts/log_counts [B, nodes, P] (log_counts = log(count) or -inf);
+ * range_starts/range_ends int64 [nodes, P] or NULL.  prototypes must be 1, 2
+ * or 4 (sparse/config.py:8); block_size >= 1.  The caller passes a device
+ * workspace of spruce_kv_summary_workspace_bytes() bytes, 16-byte aligned.
+ */
+SPRUCE_API int64_t spruce_kv_summary_workspace_bytes(int64_t B, int64_t Hkv, int64_t T, int64_t D);
+SPRUCE_API int spruce_kv_summary_table(const void *key, const int64_t key_strides[4], const void *value,
+                                       const int64_t value_strides[4], const uint8_t *valid, int dtype, int64_t B,
+                                       int64_t Hkv, int64_t T, int64_t D, int64_t block_size, int64_t prototypes,
+                                       const int64_t *node_starts, const int64_t *node_ends, int64_t num_nodes,
+                                       float *keys, float *values, float *counts, float *log_counts,
+                                       int64_t *range_starts, int64_t *range_ends, void *workspace,
+                                       int64_t workspace_bytes, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

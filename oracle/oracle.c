@@ -411,6 +411,81 @@ void oracle_sparse_attention_rows(const float *q, const float *k, const float *v
     }
 }
 
+/*
+ * build_kv_summary_table, sparse/summaries.py:52-142, with the prototype
+ * token ranges of _prototype_token_ranges (:29-49).
+ *
+ * x [B, H, T, D] contiguous (key, then value), valid uint8 [B, T] or NULL.
+ * Node ranges are in blocks (ResidualTreeLayout.starts/ends).  The reference
+ * takes an fp32 cumsum of valid-masked rows (:100-114); torch's CPU cumsum
+ * accumulates in double and rounds each prefix to float, which is what the
+ * running `acc` below does.  Means are fp32 prefix differences divided by
+ * max(count, 1) (:127-129); log_counts = log(count) or -inf (:130-134), here
+ * the correctly rounded float of the double log.
+ */
+static void summary_prefix_column(const void *x, int dtype, const uint8_t *valid, int64_t T, int64_t D,
+                                  float *prefix) {
+    double acc = 0.0;
+    prefix[0] = 0.0f;
+    for (int64_t t = 0; t < T; ++t) {
+        float w = load_elem(x, dtype, (size_t)(t * D));
+        if (valid && !valid[t]) w = 0.0f * w;
+        acc += (double)w;
+        prefix[t + 1] = (float)acc;
+    }
+}
+
+void oracle_kv_summary_table(const void *key, const void *value, int dtype, const uint8_t *valid, int64_t B,
+                             int64_t H, int64_t T, int64_t D, int64_t block_size, int64_t P,
+                             const int64_t *node_starts, const int64_t *node_ends, int64_t nodes, float *keys,
+                             float *values, float *counts, float *log_counts, int64_t *range_starts,
+                             int64_t *range_ends) {
+    for (int64_t n = 0; n < nodes; ++n) {
+        int64_t ts = node_starts[n] * block_size, te = node_ends[n] * block_size;
+        if (ts > T) ts = T;
+        if (te > T) te = T;
+        const int64_t len = te - ts;
+        for (int64_t p = 0; p < P; ++p) {
+            range_starts[n * P + p] = ts + len * p / P;
+            range_ends[n * P + p] = ts + len * (p + 1) / P;
+        }
+    }
+    const size_t es = dtype == DT_F32 ? 4 : 2;
+    for (int64_t b = 0; b < B; ++b) {
+        const uint8_t *vb = valid ? valid + b * T : NULL;
+        /* count prefix: double cumsum of 0/1 values, exact integers */
+        int64_t *cprefix = (int64_t *)malloc((size_t)(T + 1) * sizeof(int64_t));
+        cprefix[0] = 0;
+        for (int64_t t = 0; t < T; ++t) cprefix[t + 1] = cprefix[t] + (vb ? (vb[t] != 0) : 1);
+        for (int64_t i = 0; i < nodes * P; ++i) {
+            const float c = (float)(cprefix[range_ends[i]] - cprefix[range_starts[i]]);
+            counts[b * nodes * P + i] = c;
+            log_counts[b * nodes * P + i] = c > 0.0f ? (float)log((double)c) : -INFINITY;
+        }
+        free(cprefix);
+#ifdef _OPENMP
+#pragma omp parallel for collapse(2) schedule(static)
+#endif
+        for (int64_t h = 0; h < H; ++h) {
+            for (int64_t d = 0; d < D; ++d) {
+                float *prefix = (float *)malloc((size_t)(T + 1) * sizeof(float));
+                for (int which = 0; which < 2; ++which) {
+                    const char *src = (const char *)(which ? value : key) + ((b * H + h) * T * D + d) * es;
+                    float *dst = which ? values : keys;
+                    summary_prefix_column(src, dtype, vb, T, D, prefix);
+                    for (int64_t i = 0; i < nodes * P; ++i) {
+                        float c = counts[b * nodes * P + i];
+                        if (c < 1.0f) c = 1.0f;
+                        const float pooled = prefix[range_ends[i]] - prefix[range_starts[i]];
+                        dst[((b * H + h) * nodes * P + i) * D + d] = pooled / c;
+                    }
+                }
+                free(prefix);
+            }
+        }
+    }
+}
+
 /* Number of threads the OpenMP runtime will use (for the CPU-baseline report). */
 int oracle_num_threads(void) {
 #ifdef _OPENMP

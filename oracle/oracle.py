@@ -12,6 +12,8 @@ reference's sparse-prefill path end to end:
   selected_ids_to_blocks scripts/export_selected_blocks.py:80-175
   validate_selected_blocks interfaces/validator.py:7-62
   sparse attention       sparse/attention.py:143-274
+  residual tree layout   interfaces/residual_summaries.py:73-122
+  K/V summary table      sparse/summaries.py:29-142
 
 Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs import
 this module; the product path never does.  Parity is pinned by the golden
@@ -61,6 +63,8 @@ def lib():
         L.oracle_pack_ids.restype = ctypes.c_int
         L.oracle_sparse_attention.argtypes = [P, P, P, P, I64, I64, I64, I64, I64, I64, I64, F, P]
         L.oracle_sparse_attention_rows.argtypes = [P, P, P, P, I64, I64, I64, I64, I64, I64, I64, F, I64, I64, P]
+        L.oracle_kv_summary_table.argtypes = [P, P, ctypes.c_int, P, I64, I64, I64, I64, I64, I64, P, P, I64,
+                                              P, P, P, P, P, P]
         L.oracle_num_threads.restype = ctypes.c_int
         _lib = L
     return _lib
@@ -252,3 +256,50 @@ def dense_causal_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) ->
     mask = torch.ones(T, T, dtype=torch.bool).triu(1)
     s = s.masked_fill(mask, float("-inf"))
     return (torch.softmax(s, dim=-1) @ vv).transpose(1, 2).float()
+
+
+def residual_tree_ranges(num_leaves: int) -> tuple[list[int], list[int]]:
+    """Leaf-first binary-tree node ranges in blocks (interfaces/residual_summaries.py:73-122).
+
+    Level 0 holds the leaves [i, i+1); each higher level pairs neighbours
+    (an odd tail is carried up alone) until one root remains.
+    """
+    if num_leaves < 1:
+        raise ValueError(f"num_leaves must be >= 1, got {num_leaves}")
+    level = [(i, i + 1) for i in range(num_leaves)]
+    starts, ends = [], []
+    while True:
+        starts += [a for a, _ in level]
+        ends += [b for _, b in level]
+        if len(level) == 1:
+            return starts, ends
+        level = [(level[i][0], level[min(i + 1, len(level) - 1)][1]) for i in range(0, len(level), 2)]
+
+
+def kv_summary_table(key: torch.Tensor, value: torch.Tensor, starts, ends, block_size: int, prototypes: int,
+                     token_mask: torch.Tensor | None = None) -> dict:
+    """build_kv_summary_table (sparse/summaries.py:52-142) on CPU.
+
+    key/value [B, H, T, D]; starts/ends: node ranges in blocks.  Returns keys,
+    values [B, H, nodes, P, D] fp32, counts/log_counts [B, nodes, P] fp32 and
+    range_starts/range_ends [nodes, P] int64.
+    """
+    B, H, T, D = key.shape
+    nodes, P = len(starts), int(prototypes)
+    kr, vr = _raw(key), _raw(value)
+    valid = None if token_mask is None else token_mask.detach().cpu().to(torch.uint8).contiguous()
+    st = torch.tensor(list(starts), dtype=torch.int64)
+    en = torch.tensor(list(ends), dtype=torch.int64)
+    out = {
+        "keys": torch.empty((B, H, nodes, P, D), dtype=torch.float32),
+        "values": torch.empty((B, H, nodes, P, D), dtype=torch.float32),
+        "counts": torch.empty((B, nodes, P), dtype=torch.float32),
+        "log_counts": torch.empty((B, nodes, P), dtype=torch.float32),
+        "range_starts": torch.empty((nodes, P), dtype=torch.int64),
+        "range_ends": torch.empty((nodes, P), dtype=torch.int64),
+    }
+    lib().oracle_kv_summary_table(_ptr(kr), _ptr(vr), DT_CODE[key.dtype], None if valid is None else _ptr(valid),
+                                  B, H, T, D, block_size, P, _ptr(st), _ptr(en), nodes,
+                                  *(_ptr(out[n]) for n in ("keys", "values", "counts", "log_counts",
+                                                           "range_starts", "range_ends")))
+    return out

@@ -48,6 +48,9 @@ SIGNATURES = {
     "spruce_select_blocks_noalloc": ([_P, _P, _P, _P, _INT, _I64, _I64, _I64, _I64, _I64, _P, _P, _I64, _I64,
                                       _I64, _I64, _P, _P, _P], _INT),
     "spruce_select_noalloc_max_scratch_bytes": ([], _I64),
+    "spruce_kv_summary_workspace_bytes": ([_I64, _I64, _I64, _I64], _I64),
+    "spruce_kv_summary_table": ([_P, _P, _P, _P, _P, _INT, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _I64,
+                                 _P, _P, _P, _P, _P, _P, _P, _I64, _P], _INT),
     "spruce_ipc_export": ([_P, _P, ctypes.POINTER(ctypes.c_int64)], _INT),
     "spruce_ipc_import": ([_P, _I64, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p)], _INT),
     "spruce_ipc_close": ([_P], _INT),

@@ -486,4 +486,68 @@ int spruce_sparse_attention_fwd(const void* q, const int64_t q_strides[4], const
                                           status, stream);
 }
 
+int64_t spruce_kv_summary_workspace_bytes(int64_t B, int64_t Hkv, int64_t T, int64_t D) {
+  if (B < 0 || Hkv < 0 || T < 0 || D < 0) return -1;
+  return spruce::kv_summary_workspace_bytes(B, Hkv, T, D);
+}
+
+int spruce_kv_summary_table(const void* key, const int64_t key_strides[4], const void* value,
+                            const int64_t value_strides[4], const uint8_t* valid, int dtype, int64_t B, int64_t Hkv,
+                            int64_t T, int64_t D, int64_t block_size, int64_t prototypes, const int64_t* node_starts,
+                            const int64_t* node_ends, int64_t num_nodes, float* keys, float* values, float* counts,
+                            float* log_counts, int64_t* range_starts, int64_t* range_ends, void* workspace,
+                            int64_t workspace_bytes, void* stream) {
+  if (!valid_dtype(dtype)) return fail(SPRUCE_ERR_INVALID, "unsupported dtype code %d", dtype);
+  if (block_size < 1) return fail(SPRUCE_ERR_INVALID, "block_size must be positive, got %lld", (long long)block_size);
+  if (prototypes != 1 && prototypes != 2 && prototypes != 4)
+    return fail(SPRUCE_ERR_INVALID, "prototypes must be one of (1, 2, 4), got %lld", (long long)prototypes);
+  if (B < 0 || Hkv < 0 || T < 1 || D < 1 || num_nodes < 0) return fail(SPRUCE_ERR_INVALID, "bad shape");
+  if (key_strides[3] != 1 || value_strides[3] != 1)
+    return fail(SPRUCE_ERR_UNSUPPORTED, "key/value need a unit last stride");
+  if (B > 65535 || 2 * B * Hkv + B > 65535 || T > (int64_t)INT32_MAX - 16 || D > 65536 ||
+      block_size > INT32_MAX || (T / 16 + 1) * D >= (int64_t)INT32_MAX - 256)
+    return fail(SPRUCE_ERR_UNSUPPORTED, "summary table shape too large");
+  const int64_t need = spruce::kv_summary_workspace_bytes(B, Hkv, T, D);
+  if (workspace_bytes < need || (need > 0 && (workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) & 15u))))
+    return fail(SPRUCE_ERR_WORKSPACE, "workspace needs %lld bytes (16-byte aligned), got %lld", (long long)need,
+                (long long)workspace_bytes);
+  if (B == 0 || Hkv == 0 || num_nodes == 0) return SPRUCE_OK;
+  spruce::KvSummaryArgs a{};
+  a.key = key;
+  a.value = value;
+  for (int i = 0; i < 3; ++i) {
+    a.ks[i] = key_strides[i];
+    a.vs[i] = value_strides[i];
+  }
+  a.valid = valid;
+  a.B = (int)B;
+  a.H = (int)Hkv;
+  a.T = (int)T;
+  a.D = (int)D;
+  a.P = (int)prototypes;
+  a.block_size = block_size;
+  a.node_starts = node_starts;
+  a.node_ends = node_ends;
+  a.nodes = num_nodes;
+  a.out_keys = keys;
+  a.out_values = values;
+  a.out_counts = counts;
+  a.out_log_counts = log_counts;
+  a.range_starts = range_starts;
+  a.range_ends = range_ends;
+  a.prefix = static_cast<double*>(workspace);
+  a.cprefix = reinterpret_cast<int64_t*>(static_cast<char*>(workspace) +
+                                         2 * B * Hkv * (spruce::kv_summary_segments(T) + 1) * D * 8);  // 16-token worst case
+  const bool vec = aligned16(key) && aligned16(value) && vec_strides_ok(key_strides, dtype, D) &&
+                   vec_strides_ok(value_strides, dtype, D);
+  a.seg = spruce::kv_summary_segment_tokens(block_size, (int)prototypes, vec ? D / (16 / elem_size(dtype)) : D);
+  cudaError_t e;
+  switch (dtype) {
+    case SPRUCE_DTYPE_F32: e = spruce::launch_kv_summary<float>(a, vec, as_stream(stream)); break;
+    case SPRUCE_DTYPE_BF16: e = spruce::launch_kv_summary<__nv_bfloat16>(a, vec, as_stream(stream)); break;
+    default: e = spruce::launch_kv_summary<__half>(a, vec, as_stream(stream)); break;
+  }
+  return cuda_status(e, "summary table launch");
+}
+
 }  // extern "C"

@@ -68,4 +68,31 @@ cudaError_t launch_attn_f32(const AttnArgs& a, cudaStream_t stream);
 // Largest row width the tcgen05 kernel accepts for this head dim.
 int attn_sm100_max_kw(int D);
 
+// K/V summary table of the residual tree (summaries.cu).
+struct KvSummaryArgs {
+  const void* key;            // [B, H, T, D] strided, unit last stride
+  const void* value;
+  int64_t ks[3], vs[3];       // element strides b, h, t
+  const uint8_t* valid;       // [B, T] or null (every token valid)
+  int B, H, T, D, P;
+  int seg;                    // tokens per prefix segment
+  int64_t block_size;
+  const int64_t* node_starts; // [nodes] in blocks
+  const int64_t* node_ends;
+  int64_t nodes;
+  float* out_keys;            // [B, H, nodes, P, D]
+  float* out_values;
+  float* out_counts;          // [B, nodes, P]
+  float* out_log_counts;
+  int64_t* range_starts;      // [nodes, P] or null
+  int64_t* range_ends;
+  double* prefix;             // workspace: [2][B*H][nseg + 1][D]
+  int64_t* cprefix;           // workspace: [B][nseg + 1]
+};
+int64_t kv_summary_segments(int64_t T);
+int kv_summary_segment_tokens(int64_t block_size, int P, int64_t vecs_per_row);
+int64_t kv_summary_workspace_bytes(int64_t B, int64_t H, int64_t T, int64_t D);
+template <typename T>
+cudaError_t launch_kv_summary(const KvSummaryArgs& a, bool vec, cudaStream_t stream);
+
 }  // namespace spruce

@@ -266,3 +266,43 @@ def ipc_import(handle: bytes, offset: int) -> tuple[int, int]:
 
 def ipc_close(base: int) -> None:
     _lib.check(_lib.load().spruce_ipc_close(base))
+
+
+def kv_summary_table(key: torch.Tensor, value: torch.Tensor, node_starts: torch.Tensor, node_ends: torch.Tensor,
+                     block_size: int, prototypes: int, valid: torch.Tensor | None = None) -> dict:
+    """Per-node prototype means of K and V (sparse/summaries.py:52-142).
+
+    key/value [B, Hkv, T, D] CUDA tensors of one dtype; node_starts/node_ends
+    int64 block ranges on the same device; valid bool/uint8 [B, T] or None.
+    Returns the fp32 keys/values [B, Hkv, nodes, P, D], counts/log_counts
+    [B, nodes, P] and int64 range_starts/range_ends [nodes, P].
+    """
+    _lib.require_cuda(key, value, node_starts, node_ends)
+    if key.dtype != value.dtype:
+        raise ValueError(f"key/value dtype mismatch: {key.dtype} vs {value.dtype}")
+    B, H, T, D = key.shape
+    nodes, P = node_starts.numel(), int(prototypes)
+    dev = key.device
+    key = key if key.stride(-1) == 1 else key.contiguous()
+    value = value if value.stride(-1) == 1 else value.contiguous()
+    st = node_starts.to(device=dev, dtype=torch.int64).contiguous()
+    en = node_ends.to(device=dev, dtype=torch.int64).contiguous()
+    vmask = None if valid is None else valid.to(device=dev, dtype=torch.uint8).contiguous()
+    L = _lib.load()
+    ws_bytes = int(L.spruce_kv_summary_workspace_bytes(B, H, T, D))
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+    out = {
+        "keys": torch.empty((B, H, nodes, P, D), dtype=torch.float32, device=dev),
+        "values": torch.empty((B, H, nodes, P, D), dtype=torch.float32, device=dev),
+        "counts": torch.empty((B, nodes, P), dtype=torch.float32, device=dev),
+        "log_counts": torch.empty((B, nodes, P), dtype=torch.float32, device=dev),
+        "range_starts": torch.empty((nodes, P), dtype=torch.int64, device=dev),
+        "range_ends": torch.empty((nodes, P), dtype=torch.int64, device=dev),
+    }
+    _lib.check(L.spruce_kv_summary_table(
+        key.data_ptr(), _lib.strides(key), value.data_ptr(), _lib.strides(value),
+        None if vmask is None else vmask.data_ptr(), _dt(key), B, H, T, D, block_size, P,
+        st.data_ptr(), en.data_ptr(), nodes, out["keys"].data_ptr(), out["values"].data_ptr(),
+        out["counts"].data_ptr(), out["log_counts"].data_ptr(), out["range_starts"].data_ptr(),
+        out["range_ends"].data_ptr(), ws.data_ptr(), ws_bytes, _lib.stream_of(key)))
+    return out

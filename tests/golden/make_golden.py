@@ -6,7 +6,9 @@ Run in a container that has the reference checkout (read-only is fine):
 
 It imports the reference's own torch functions -- _group_avg_tokens,
 _proto_pool_seq, FlatGate, selected_ids_to_blocks, validate_selected_blocks,
-sparse_prefill_attention_forward -- feeds them the seeded synthetic inputs of
+sparse_prefill_attention_forward, build_kv_summary_table,
+build_residual_tree_layout, build_residual_summary_nodes,
+residual_attention_density -- feeds them the seeded synthetic inputs of
 spruce_research_b200.synthetic and stores their outputs as .npz fixtures.
 The tests regenerate the inputs from the stored seeds (checked against the
 stored input checksums) and compare the oracle and the CUDA path with the
@@ -119,9 +121,75 @@ def proto_cases(ref):
     return cases
 
 
+# name: (shape, dtype, seed, rope, block_size, prototypes, mask kind, stored nodes (None = all))
+SUMMARY_CASES = {
+    "sum_ragged_bf16": (LayerShape(1, 4, 2, 357, 64), torch.bfloat16, 2, 1e6, 64, 4, None, None),
+    "sum_batch2_f32": (LayerShape(2, 4, 1, 256, 128), torch.float32, 4, 1e6, 64, 2, "holes", None),
+    "sum_c0_f32": (LayerShape(1, 4, 2, 4096, 64), torch.float32, 0, None, 64, 1, None, None),
+    "sum_c1_8k_bf16": (LayerShape(1, 28, 4, 8192, 128), torch.bfloat16, 5, 1e6, 64, 4, None, (0, 1, 127, 200, 254)),
+    "sum_gqa_fp16_bs16": (LayerShape(1, 14, 2, 320, 128), torch.float16, 3, 1e6, 16, 4, "right_pad", None),
+}
+
+
+def summary_mask(kind, B, T):
+    if kind is None:
+        return None
+    m = torch.ones((B, T), dtype=torch.bool)
+    if kind == "holes":
+        m[0, 10:12] = False
+        m[0, 100:111] = False
+        m[-1, 200:] = False
+    else:  # right padding of the last batch item
+        m[-1, T - 37:] = False
+    return m
+
+
+def summary_cases(ref):
+    import hashlib
+
+    cases = {}
+    for name, (shape, dtype, seed, rope, bs, P, mask_kind, keep) in SUMMARY_CASES.items():
+        _, k, v = make_layer_inputs(shape, dtype, seed, rope_theta=rope)
+        mask = summary_mask(mask_kind, shape.batch, shape.tokens)
+        layout = ref["tree_layout"]((shape.tokens + bs - 1) // bs)
+        t = ref["summary"](k, v, layout, block_size=bs, prototypes=P, token_mask=mask)
+        nodes = np.arange(layout.num_nodes) if keep is None else np.array(keep)
+        cases[f"{name}_args"] = np.array([shape.batch, shape.q_heads, shape.kv_heads, shape.tokens, shape.head_dim,
+                                          {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}[dtype], seed,
+                                          bs, P], dtype=np.int64)
+        cases[f"{name}_rope"] = np.array([rope or 0.0])
+        cases[f"{name}_mask"] = np.array([{None: 0, "holes": 1, "right_pad": 2}[mask_kind]])
+        cases[f"{name}_nodes"] = nodes
+        cases[f"{name}_keys"] = t.keys[:, :, nodes].numpy()
+        cases[f"{name}_values"] = t.values[:, :, nodes].numpy()
+        cases[f"{name}_counts"] = t.counts.numpy()
+        cases[f"{name}_log_counts"] = t.log_counts.numpy()
+        cases[f"{name}_range_starts"] = t.range_starts.numpy()
+        cases[f"{name}_range_ends"] = t.range_ends.numpy()
+        digest = hashlib.sha256()
+        for a in (t.keys, t.values, t.counts):
+            digest.update(a.contiguous().numpy().tobytes())
+        cases[f"{name}_sha256"] = np.frombuffer(digest.digest(), dtype=np.uint8)
+        print(f"{name}: nodes={layout.num_nodes} P={P} keys {tuple(t.keys.shape)}")
+    # tree layouts and maximal frontiers (interfaces/residual_summaries.py)
+    for n in (1, 2, 3, 5, 7, 64, 100):
+        lay = ref["tree_layout"](n)
+        cases[f"tree{n}"] = np.array([lay.starts, lay.ends, lay.levels, lay.indices], dtype=np.int64)
+        cases[f"tree{n}_counts"] = np.array(lay.level_counts, dtype=np.int64)
+    c0 = np.load(os.path.join(HERE, "c0.npz"))
+    selected = torch.from_numpy(c0["selected"])[:, None].contiguous()    # [B, 1, G, qb, K]
+    nodes = ref["summary_nodes"](selected, validate_selected=False)  # c0 routes use local_window=0
+    cases["frontier_c0"] = nodes.numpy()
+    dens = ref["summary_density"](selected, nodes, seq_len=4096, block_size=64, prototypes=4)
+    cases["frontier_c0_density"] = np.array([dens["exact_attention_entries"], dens["summary_prototype_entries"],
+                                             dens["maximum_causal_attention_entries"]], dtype=np.int64)
+    return cases
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("SPRUCE_REFERENCE", "/root/reference"))
+    ap.add_argument("--only", choices=["all", "summaries"], default="all")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     from teacher.chunked_extract import _group_avg_tokens, _proto_pool_seq
@@ -129,10 +197,17 @@ def main():
     from scripts.export_selected_blocks import selected_ids_to_blocks
     from interfaces.validator import validate_selected_blocks
     from sparse.attention import sparse_prefill_attention_forward
+    from sparse.summaries import build_kv_summary_table, residual_attention_density
+    from interfaces.residual_summaries import build_residual_summary_nodes, build_residual_tree_layout
     ref = {"group_avg": _group_avg_tokens, "proto_pool": _proto_pool_seq, "FlatGate": FlatGate,
            "pack": selected_ids_to_blocks, "validate": validate_selected_blocks,
-           "attention": sparse_prefill_attention_forward}
+           "attention": sparse_prefill_attention_forward, "summary": build_kv_summary_table,
+           "tree_layout": build_residual_tree_layout, "summary_nodes": build_residual_summary_nodes,
+           "summary_density": residual_attention_density}
     torch.set_num_threads(max(1, os.cpu_count() or 1))
+    if args.only == "summaries":
+        np.savez_compressed(os.path.join(HERE, "summaries.npz"), **summary_cases(ref))
+        return
 
     for name, (shape, dtype, seed, rope, K, lw, sink, keep_blocks) in CASES.items():
         q, k, v = make_layer_inputs(shape, dtype, seed, rope_theta=rope)
@@ -162,6 +237,7 @@ def main():
 
     np.savez_compressed(os.path.join(HERE, "packing.npz"), **packing_cases(ref))
     np.savez_compressed(os.path.join(HERE, "proto.npz"), **proto_cases(ref))
+    np.savez_compressed(os.path.join(HERE, "summaries.npz"), **summary_cases(ref))
     print("wrote", sorted(f for f in os.listdir(HERE) if f.endswith(".npz")))
 
 

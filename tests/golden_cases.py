@@ -65,3 +65,68 @@ def load_case(name: str) -> GoldenCase:
 
 def load_npz(name: str) -> dict:
     return dict(np.load(os.path.join(HERE, f"{name}.npz")))
+
+
+SUMMARY_CASE_NAMES = ["sum_ragged_bf16", "sum_batch2_f32", "sum_c0_f32", "sum_c1_8k_bf16", "sum_gqa_fp16_bs16"]
+
+
+@dataclass
+class SummaryCase:
+    """One build_kv_summary_table fixture of summaries.npz (reference outputs)."""
+
+    name: str
+    shape: LayerShape
+    dtype: torch.dtype
+    seed: int
+    rope: float | None
+    block_size: int
+    prototypes: int
+    mask_kind: int
+    z: dict
+
+    def inputs(self, device="cpu"):
+        """(key, value, token_mask) as the generator made them; K/V keep the [B, T, H, D] storage."""
+        _, k, v = make_layer_inputs(self.shape, self.dtype, self.seed, rope_theta=self.rope)
+        mask = None
+        if self.mask_kind:
+            B, T = self.shape.batch, self.shape.tokens
+            mask = torch.ones((B, T), dtype=torch.bool)
+            if self.mask_kind == 1:
+                mask[0, 10:12] = False
+                mask[0, 100:111] = False
+                mask[-1, 200:] = False
+            else:
+                mask[-1, T - 37:] = False
+        if device != "cpu":
+            k = k.transpose(1, 2).contiguous().to(device).transpose(1, 2)
+            v = v.transpose(1, 2).contiguous().to(device).transpose(1, 2)
+            mask = None if mask is None else mask.to(device)
+        return k, v, mask
+
+    def get(self, key: str) -> torch.Tensor:
+        return torch.from_numpy(np.ascontiguousarray(self.z[f"{self.name}_{key}"]))
+
+    @property
+    def nodes(self) -> torch.Tensor:
+        return self.get("nodes")
+
+    @property
+    def sha256(self) -> bytes:
+        return bytes(self.z[f"{self.name}_sha256"].tolist())
+
+
+def load_summary_case(name: str) -> SummaryCase:
+    z = load_npz("summaries")
+    B, Hq, Hkv, T, D, dt, seed, bs, P = (int(x) for x in z[f"{name}_args"])
+    rope = float(z[f"{name}_rope"][0]) or None
+    return SummaryCase(name, LayerShape(B, Hq, Hkv, T, D), DT[dt], seed, rope, bs, P,
+                       int(z[f"{name}_mask"][0]), z)
+
+
+def table_sha256(keys: torch.Tensor, values: torch.Tensor, counts: torch.Tensor) -> bytes:
+    import hashlib
+
+    h = hashlib.sha256()
+    for a in (keys, values, counts):
+        h.update(a.detach().cpu().contiguous().numpy().tobytes())
+    return h.digest()
