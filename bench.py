@@ -332,23 +332,18 @@ def run_b200(args):
         hk = k[:, g0:g1].transpose(1, 2).contiguous().cpu().pin_memory()
         hv = v[:, g0:g1].transpose(1, 2).contiguous().cpu().pin_memory()
         dq, dk, dv = (torch.empty_like(t, device=dev) for t in (hq, hk, hv))
-        hout = torch.empty((B, T, shape.q_heads, D), dtype=torch.bfloat16).pin_memory() if rank == 0 else None
+        # each rank reads back the rows and heads it computed: over all ranks, the whole output
+        hout = torch.empty((B, T, (g1 - g0) * rep, D), dtype=torch.bfloat16).pin_memory()
         streamer = HostStreamedLayer(layer, dev, chunks=args.e2e_chunks)
 
         def e2e_step():
             # H2D of chunk c+1, selector + attention of chunk c and D2H of chunk c-1 overlap
-            if world == 1:
-                streamer(hq, hk, hv, dq, dk, dv, local_out, hout=hout, q_blocks=(i0, i1))
-                return
-            streamer(hq, hk, hv, dq, dk, dv, local_out, q_blocks=(i0, i1), peer_outs=peer_ptrs)
-            full = local_out
-            if fused:
-                peer.fence()
-                full = peer.local
-            else:
-                full = runner.gather(local_out[:, i0 * 64:i1 * 64], shape.kv_heads, T)
-            if rank == 0:
-                hout.copy_(full, non_blocking=True)
+            streamer(hq, hk, hv, dq, dk, dv, local_out, hout=hout, q_blocks=(i0, i1), peer_outs=peer_ptrs)
+            if world > 1:  # the on-device all-gather completes as part of the step
+                if fused:
+                    peer.fence()
+                else:
+                    runner.gather(local_out[:, i0 * 64:i1 * 64], shape.kv_heads, T)
 
         for _ in range(max(1, args.warmup)):
             e2e_step()
@@ -360,12 +355,16 @@ def run_b200(args):
         e1.record()
         barrier()
         e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+        moved = torch.tensor([streamer.h2d_bytes, streamer.d2h_bytes], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(moved)
         e2e = {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
-               "h2d_bytes_per_step": int(sum(t.numel() * t.element_size() for t in (hq, hk, hv))),
-               "d2h_bytes_per_step": int(hout.numel() * hout.element_size()) if rank == 0 else 0,
+               "h2d_bytes_per_step": int(moved[0].item()), "d2h_bytes_per_step": int(moved[1].item()),
                "path": ("pinned host Q/K/V -> HostStreamedLayer (copies of chunk c+1, selector + attention of "
                         f"chunk c and copy-back of chunk c-1 overlap; {args.e2e_chunks} query-block chunks) -> "
-                        "pinned host output")}
+                        "pinned host output" + ("" if world == 1 else
+                                                "; each rank copies its own query rows, the K/V rows they "
+                                                "attend and its output shard (bytes summed over ranks)"))}
         del dq, dk, dv
 
     # ---- CPU baseline (rank 0, single GPU only)

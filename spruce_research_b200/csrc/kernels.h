@@ -29,7 +29,7 @@ cudaError_t launch_project_rows(const void* x, int64_t groups, int qb, int row0,
 
 cudaError_t launch_scores(const float* qp, const float* kp, int64_t R, int qb, int kb, int P, float* out,
                           cudaStream_t stream);
-int select_rows_for(int qb, int P);
+int select_rows_for(int qb, int P, int64_t tiles16 = -1);
 cudaError_t launch_select(const float* qp, const float* kp, int B, int G, int qb, int P, int K, int lw, int sink,
                           int32_t* out, const int64_t* out_strides, int q_begin, int q_end, cudaStream_t stream);
 cudaError_t launch_pack_ids(const int64_t* ids, int64_t R, int qb, int C, int K, int lw, int kb, int sink,

@@ -19,9 +19,13 @@
 namespace spruce {
 
 // ------------------------------------------------------------------ projection
-constexpr int kProjRows = 8;
 
 // Row n of the launch is row (n / nrows) * qb + row0 + n % nrows of x (and of out).
+// kProjRows rows per 128-thread CTA: the rows are staged in shared memory,
+// thread p keeps one accumulator per row and reads 16 weights at a time.
+// Each output is one fma chain over d = 0..D-1 in order.
+constexpr int kProjRows = 4;
+
 template <typename T>
 __global__ void __launch_bounds__(128) project_kernel(const T* __restrict__ x, int64_t N, int D,
                                                       const float* __restrict__ W, int P, float* __restrict__ out,
@@ -31,18 +35,60 @@ __global__ void __launch_bounds__(128) project_kernel(const T* __restrict__ x, i
   const int rows = (int)(N - n0 < kProjRows ? N - n0 : kProjRows);
   auto map_row = [&](int64_t n) { return (n / nrows) * qb + row0 + n % nrows; };
   for (int e = threadIdx.x; e < rows * D; e += blockDim.x) xs[e] = Elem<T>::to_f(x[map_row(n0 + e / D) * D + e % D]);
+  for (int e = rows * D + threadIdx.x; e < kProjRows * D; e += blockDim.x) xs[e] = 0.0f;
   __syncthreads();
   for (int p = threadIdx.x; p < P; p += blockDim.x) {
     float acc[kProjRows];
 #pragma unroll
     for (int r = 0; r < kProjRows; ++r) acc[r] = 0.0f;
-    for (int d = 0; d < D; ++d) {
+    int d = 0;
+    for (; d + 16 <= D; d += 16) {  // 16 weight loads in flight, then the chains in d order
+      float w[16];
+#pragma unroll
+      for (int u = 0; u < 16; ++u) w[u] = __ldg(W + (int64_t)(d + u) * P + p);
+#pragma unroll
+      for (int u = 0; u < 16; ++u)
+#pragma unroll
+        for (int r = 0; r < kProjRows; ++r) acc[r] = __fmaf_rn(xs[r * D + d + u], w[u], acc[r]);
+    }
+    for (; d < D; ++d) {
       const float w = __ldg(W + (int64_t)d * P + p);
 #pragma unroll
       for (int r = 0; r < kProjRows; ++r) acc[r] = __fmaf_rn(xs[r * D + d], w, acc[r]);
     }
     for (int r = 0; r < rows; ++r) out[map_row(n0 + r) * P + p] = acc[r];
   }
+}
+
+// The same projection with one thread per output (row, p), for few rows: a
+// row-tiled CTA per 4 rows would leave most SMs idle, while per-output
+// threads spread the (tiny) work over every SM.  128-thread blocks along p,
+// so a warp shares its row (broadcast loads of x) and reads 32 consecutive
+// weights; one fma chain over d = 0..D-1 in order per output.
+template <typename T>
+__global__ void __launch_bounds__(128) project_out_kernel(const T* __restrict__ x, int64_t N, int D,
+                                                          const float* __restrict__ W, int P,
+                                                          float* __restrict__ out, int qb, int row0, int nrows) {
+  const int64_t idx = (int64_t)blockIdx.x * 128 + threadIdx.x;
+  if (idx >= N * P) return;
+  const int p = (int)(idx % P);
+  const int64_t n = idx / P;
+  const int64_t row = (n / nrows) * qb + row0 + n % nrows;
+  const T* xr = x + row * D;
+  float acc = 0.0f;
+  int d = 0;
+  for (; d + 8 <= D; d += 8) {  // 16 loads in flight, then the chain in d order
+    float xv[8], wv[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      xv[u] = Elem<T>::to_f(xr[d + u]);
+      wv[u] = __ldg(W + (int64_t)(d + u) * P + p);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) acc = __fmaf_rn(xv[u], wv[u], acc);
+  }
+  for (; d < D; ++d) acc = __fmaf_rn(Elem<T>::to_f(xr[d]), __ldg(W + (int64_t)d * P + p), acc);
+  out[row * P + p] = acc;
 }
 
 // ------------------------------------------------------------------ score tiles
@@ -154,6 +200,96 @@ __device__ __forceinline__ void score_tile16(const float* qs, int qstride, const
   }
 }
 
+// 16-byte asynchronous global->shared copy; src_bytes = 0 writes zeros.
+__device__ __forceinline__ void cp_async16(float* dst, const float* src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// 4*RM query rows against all column chunks [0, ncols), RM x 4 register
+// micro-tiles (thread t: rows RM*(t/64).., columns j0 + t%64 + 64c), with the
+// key projections staged by cp.async into two alternating buffers
+// (ks2: 2 x [256][kKStride]): the copy of stage s+1 (a 256-column x 32-p
+// slab) is in flight while stage s is multiplied.  Every score is one fma
+// chain over p = 0..P-1 in order, as in score_tile16 / score_columns, so the
+// scores are bit-identical.  Needs P % 4 == 0 (16-byte aligned key rows).
+template <int RM, typename Emit>
+__device__ __forceinline__ void score_rows_async(const float* qs, int qstride, const float* __restrict__ kp,
+                                                 int P, int ncols, float* ks2, float denom, Emit emit) {
+  const int t = threadIdx.x;
+  const int rg = t >> 6;
+  const int cg = t & 63;
+  const int npc = (P + kPChunk - 1) / kPChunk;
+  const int total = ((ncols + kScoreThreads - 1) / kScoreThreads) * npc;
+  if (total == 0) return;
+  auto issue = [&](int st) {
+    const int j0 = (st / npc) * kScoreThreads, p0 = (st % npc) * kPChunk;
+    float* buf = ks2 + (st & 1) * (kScoreThreads * kKStride);
+#pragma unroll
+    for (int i = 0; i < kPChunk * kScoreThreads / 4 / kScoreThreads; ++i) {
+      const int e = t + kScoreThreads * i;
+      const int jj = e >> 3, part = e & 7;
+      const int j = j0 + jj, p = p0 + part * 4;
+      const bool ok = j < ncols && p < P;
+      cp_async16(buf + jj * kKStride + part * 4, ok ? kp + (int64_t)j * P + p : kp, ok ? 16 : 0);
+    }
+    cp_async_commit();
+  };
+  issue(0);
+  float acc[RM][4];
+#pragma unroll
+  for (int r = 0; r < RM; ++r)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) acc[r][c] = 0.0f;
+  for (int st = 0; st < total; ++st) {
+    if (st + 1 < total) {
+      issue(st + 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const float* ks = ks2 + (st & 1) * (kScoreThreads * kKStride);
+    const int pc = st % npc;
+    const int p0 = pc * kPChunk;
+    const int pn = min(kPChunk, P - p0);
+    for (int pp = 0; pp < pn; pp += 4) {
+      float4 qv[RM], kv[4];
+#pragma unroll
+      for (int r = 0; r < RM; ++r) qv[r] = *reinterpret_cast<const float4*>(qs + (RM * rg + r) * qstride + p0 + pp);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) kv[c] = *reinterpret_cast<const float4*>(ks + (cg + 64 * c) * kKStride + pp);
+#pragma unroll
+      for (int r = 0; r < RM; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          acc[r][c] = __fmaf_rn(qv[r].x, kv[c].x, acc[r][c]);
+          acc[r][c] = __fmaf_rn(qv[r].y, kv[c].y, acc[r][c]);
+          acc[r][c] = __fmaf_rn(qv[r].z, kv[c].z, acc[r][c]);
+          acc[r][c] = __fmaf_rn(qv[r].w, kv[c].w, acc[r][c]);
+        }
+    }
+    if (pc == npc - 1) {
+      const int j0 = (st / npc) * kScoreThreads;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int j = j0 + cg + 64 * c;
+        if (j < ncols)
+#pragma unroll
+          for (int r = 0; r < RM; ++r) emit(RM * rg + r, j, __fdiv_rn(acc[r][c], denom));
+      }
+#pragma unroll
+      for (int r = 0; r < RM; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[r][c] = 0.0f;
+    }
+    __syncthreads();  // buffer st & 1 is refilled by the issue at the top of iteration st + 1
+  }
+}
+
 // Full score matrix (FlatGate.forward, P = 1): grid (ceil(qb/ROWS), R).
 template <int ROWS>
 __global__ void __launch_bounds__(kScoreThreads) scores_kernel(const float* __restrict__ qp,
@@ -246,7 +382,7 @@ __global__ void __launch_bounds__(kScoreThreads) select_kernel(SelectArgs a) {
   const int qstride = (P + 3) / 4 * 4 + 4;           // padded row stride of qs (16-byte aligned rows)
   float* qs = sm;                                   // [ROWS][qstride]
   float* kT = qs + ROWS * qstride;                  // staging: [256][kKStride] or [kPChunk][256]
-  int* hist = reinterpret_cast<int*>(kT + kScoreThreads * kKStride);  // [8 warps][256]
+  int* hist = reinterpret_cast<int*>(kT + (ROWS >= 8 ? 2 : 1) * kScoreThreads * kKStride);  // [8 warps][256]
   uint32_t* keys = reinterpret_cast<uint32_t*>(hist + 8 * 256);     // [ROWS][qb]
 
   const int tiles = (a.q_end - a.q_begin + ROWS - 1) / ROWS;
@@ -263,14 +399,24 @@ __global__ void __launch_bounds__(kScoreThreads) select_kernel(SelectArgs a) {
   }
   // Only candidates j < q - local_window of the tile's last row are needed.
   const int ncols = max(0, min(qb, r0 + ROWS - a.local_window));
-  for (int j0 = 0; j0 < ncols; j0 += kScoreThreads) {
-    if constexpr (ROWS == 16) {
-      score_tile16(qs, qstride, k, P, j0, ncols, kT, a.denom,
-                   [&](int r, int j, float s) { keys[r * qb + j] = order_key(s); });
+  if constexpr (ROWS == 16 || ROWS == 8) {
+    if (P % 4 == 0) {
+      __syncthreads();  // qs is complete before the first multiply
+      score_rows_async<ROWS / 4>(qs, qstride, k, P, ncols, kT, a.denom,
+                                 [&](int r, int j, float s) { keys[r * qb + j] = order_key(s); });
+    } else if constexpr (ROWS == 16) {
+      for (int j0 = 0; j0 < ncols; j0 += kScoreThreads)
+        score_tile16(qs, qstride, k, P, j0, ncols, kT, a.denom,
+                     [&](int r, int j, float s) { keys[r * qb + j] = order_key(s); });
     } else {
+      for (int j0 = 0; j0 < ncols; j0 += kScoreThreads)
+        score_columns<ROWS>(qs, k, P, j0, ncols, kT, a.denom,
+                            [&](int r, int j, float s) { keys[r * qb + j] = order_key(s); }, qstride);
+    }
+  } else {
+    for (int j0 = 0; j0 < ncols; j0 += kScoreThreads)
       score_columns<ROWS>(qs, k, P, j0, ncols, kT, a.denom,
                           [&](int r, int j, float s) { keys[r * qb + j] = order_key(s); }, qstride);
-    }
   }
   __syncthreads();
 
@@ -454,25 +600,28 @@ __global__ void validate_finish_kernel(unsigned long long* result) {
 
 // ------------------------------------------------------------------ launchers
 template <typename T>
-cudaError_t launch_project(const void* x, int64_t N, int D, const float* W, int P, float* out,
-                           cudaStream_t stream) {
-  if (N == 0) return cudaSuccess;
-  const int grid = (int)((N + kProjRows - 1) / kProjRows);
-  const size_t smem = sizeof(float) * kProjRows * D;
-  project_kernel<T><<<grid, 128, smem, stream>>>(static_cast<const T*>(x), N, D, W, P, out, (int)N, 0, (int)N);
-  return cudaGetLastError();
-}
-
-template <typename T>
 cudaError_t launch_project_rows(const void* x, int64_t groups, int qb, int row0, int nrows, int D, const float* W,
                                 int P, float* out, cudaStream_t stream) {
   const int64_t N = groups * nrows;
   if (N == 0) return cudaSuccess;
-  const int grid = (int)((N + kProjRows - 1) / kProjRows);
+  if (N * P <= (int64_t)148 * 128 * 16) {  // fewer outputs than 16 per-output threads per SM-lane
+    project_out_kernel<T><<<(unsigned)((N * P + 127) / 128), 128, 0, stream>>>(static_cast<const T*>(x), N, D, W, P,
+                                                                              out, qb, row0, nrows);
+    return cudaGetLastError();
+  }
   const size_t smem = sizeof(float) * kProjRows * D;
-  project_kernel<T><<<grid, 128, smem, stream>>>(static_cast<const T*>(x), N, D, W, P, out, qb, row0, nrows);
+  project_kernel<T><<<(unsigned)((N + kProjRows - 1) / kProjRows), 128, smem, stream>>>(
+      static_cast<const T*>(x), N, D, W, P, out, qb, row0, nrows);
   return cudaGetLastError();
 }
+
+template <typename T>
+cudaError_t launch_project(const void* x, int64_t N, int D, const float* W, int P, float* out,
+                           cudaStream_t stream) {
+  if (N > INT32_MAX) return cudaErrorInvalidValue;
+  return launch_project_rows<T>(x, 1, (int)N, 0, (int)N, D, W, P, out, stream);
+}
+
 template cudaError_t launch_project_rows<float>(const void*, int64_t, int, int, int, int, const float*, int, float*,
                                                 cudaStream_t);
 template cudaError_t launch_project_rows<__nv_bfloat16>(const void*, int64_t, int, int, int, int, const float*, int,
@@ -499,7 +648,8 @@ cudaError_t launch_scores(const float* qp, const float* kp, int64_t R, int qb, i
 
 size_t select_smem_bytes(int rows, int qb, int P) {
   const int qstride = (P + 3) / 4 * 4 + 4;
-  return sizeof(float) * (rows * qstride + kScoreThreads * kKStride) + sizeof(int) * 8 * 256 +
+  const int stages = rows >= 8 ? 2 : 1;  // 8- and 16-row tiles double-buffer the key staging
+  return sizeof(float) * (rows * qstride + stages * kScoreThreads * kKStride) + sizeof(int) * 8 * 256 +
          sizeof(uint32_t) * (size_t)rows * qb;
 }
 
@@ -514,9 +664,12 @@ static cudaError_t launch_select_rows(const SelectArgs& a, cudaStream_t stream) 
   return cudaGetLastError();
 }
 
-int select_rows_for(int qb, int P) {
-  const size_t limit = 200 * 1024;
-  if (select_smem_bytes(16, qb, P) <= limit) return 16;
+// Largest tile whose keys fit in shared memory; 16-row tiles only when they
+// still give two waves of CTAs (`tiles16` = CTAs at 16 rows, < 0 = unknown),
+// else 8-row tiles, which halve the rows per CTA and double the CTAs.
+int select_rows_for(int qb, int P, int64_t tiles16) {
+  const size_t limit = 227 * 1024;
+  if (select_smem_bytes(16, qb, P) <= limit && (tiles16 < 0 || tiles16 >= 2 * 148)) return 16;
   if (select_smem_bytes(8, qb, P) <= limit) return 8;
   if (select_smem_bytes(4, qb, P) <= limit) return 4;
   return 0;
@@ -542,7 +695,7 @@ cudaError_t launch_select(const float* qp, const float* kp, int B, int G, int qb
   a.osg = out_strides[1];
   a.osq = out_strides[2];
   a.denom = gate_denom(P);
-  switch (select_rows_for(qb, P)) {
+  switch (select_rows_for(qb, P, (int64_t)((q_end - q_begin + 15) / 16) * G * B)) {
     case 16: return launch_select_rows<16>(a, stream);
     case 8: return launch_select_rows<8>(a, stream);
     case 4: return launch_select_rows<4>(a, stream);

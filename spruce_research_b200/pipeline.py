@@ -58,6 +58,10 @@ def sparse_prefill_layer(q, k, v, wq, wk, k_selected, local_window=0, sink_block
     return SparsePrefillLayer(wq, wk, k_selected, local_window, sink_blocks)(q, k, v)
 
 
+def _nbytes(t: torch.Tensor) -> int:
+    return t.numel() * t.element_size()
+
+
 class HostStreamedLayer:
     """One layer fed from pinned host buffers, pipelined over query-block chunks.
 
@@ -84,8 +88,11 @@ class HostStreamedLayer:
                  after_attention=None, copy_out=True):
         """hq/hk/hv pinned token-major [B, T, H, D]; dq/dk/dv/dout device tensors of the same shapes.
 
+        Only query blocks ``q_blocks`` (default: all) are computed: their
+        query rows and the key/value rows up to their end are copied in.
         ``dout`` receives the layer output ([B, T, Hq, D]); with ``hout`` and
-        ``copy_out`` it is streamed back to the host chunk by chunk.
+        ``copy_out`` those rows are streamed back to the host chunk by chunk.
+        The bytes moved are left in ``h2d_bytes`` / ``d2h_bytes``.
         """
         B, T, Hq, D = hq.shape
         Hkv = hk.shape[2]
@@ -100,17 +107,19 @@ class HostStreamedLayer:
         for s in (self.h2d, self.compute, self.d2h):
             s.wait_stream(cur)
         qv, kv, vv = dq.transpose(1, 2), dk.transpose(1, 2), dv.transpose(1, 2)
-        loaded = 0  # tokens already on the device (K/V rows of earlier chunks stay resident)
+        loaded = 0  # K/V tokens already on the device (rows of earlier chunks stay resident)
+        self.h2d_bytes = self.d2h_bytes = 0
         for c in range(C):
             i0, i1 = bounds[c], bounds[c + 1]
-            t1 = min(i1 * BLOCK, T)
+            t0, t1 = i0 * BLOCK, min(i1 * BLOCK, T)
             h_done = torch.cuda.Event()
             with torch.cuda.stream(self.h2d):
-                # everything up to this chunk's last token: its queries, and keys/values it may attend
-                dq[:, loaded:t1].copy_(hq[:, loaded:t1], non_blocking=True)
+                # this chunk's queries, and every key/value row up to its last token that it may attend
+                dq[:, t0:t1].copy_(hq[:, t0:t1], non_blocking=True)
                 dk[:, loaded:t1].copy_(hk[:, loaded:t1], non_blocking=True)
                 dv[:, loaded:t1].copy_(hv[:, loaded:t1], non_blocking=True)
                 h_done.record()
+            self.h2d_bytes += _nbytes(hq[:, t0:t1]) + 2 * _nbytes(hk[:, loaded:t1])
             loaded = t1
             c_done = torch.cuda.Event()
             with torch.cuda.stream(self.compute):
@@ -123,8 +132,8 @@ class HostStreamedLayer:
             if hout is not None and copy_out:
                 with torch.cuda.stream(self.d2h):
                     self.d2h.wait_event(c_done)
-                    t0 = i0 * BLOCK
                     hout[:, t0:t1].copy_(dout[:, t0:t1], non_blocking=True)
+                self.d2h_bytes += _nbytes(hout[:, t0:t1])
         for s in (self.h2d, self.compute, self.d2h):
             cur.wait_stream(s)
         return dout
