@@ -37,8 +37,10 @@
 // TMEM columns: O_t at [t*D, (t+1)*D); S_t at 2D + 64t; P_t[b] at 2D + 128 + 64t + 32b.
 #include <algorithm>
 
-#include "common.cuh"
-#include "kernels.h"
+#include <cstdlib>
+#include <cstring>
+
+#include "attn_common.cuh"
 
 namespace spruce {
 
@@ -46,25 +48,6 @@ constexpr int kAttnThreads = 352;
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;   // QK^T issuer, owns the TMEM allocation
 constexpr int kPvWarp = 10;   // PV issuer
-
-struct AttnParams {
-  const int32_t* idx;
-  int64_t isb, isg, isq;
-  void* out;
-  int64_t osb, osh, ost;
-  int Hq, Hkv, T, Kw, qb, rep, n_pair, n_cta;
-  int q_begin, nq;  // query blocks [q_begin, q_begin + nq) are computed
-  float scale_log2;
-  uint32_t* status;
-};
-
-// Output tensor maps: [0] this GPU's output, [1..] the peers' outputs for the
-// fused all-gather (NVLink peer memory, same layout).  Box (64 dims, 1 head,
-// 64 tokens), 128-byte swizzle.
-struct OutMaps {
-  CUtensorMap m[1 + kMaxPeers];
-  int count;
-};
 
 template <int D, int STAGES>
 struct AttnLayout {
@@ -86,64 +69,6 @@ struct AttnLayout {
   static constexpr uint32_t TMEM_COLS = (2 * D + 256 <= 256) ? 256u : 512u;
   static size_t smem_bytes(int kw) { return 1024 + OFF_IDS + 4 * (size_t)kw; }
 };
-
-template <typename T> struct Pack2;
-template <> struct Pack2<__nv_bfloat16> {
-  static __device__ __forceinline__ uint32_t pack(float a, float b) {
-    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-    return *reinterpret_cast<uint32_t*>(&h);
-  }
-};
-template <> struct Pack2<__half> {
-  static __device__ __forceinline__ uint32_t pack(float a, float b) {
-    __half2 h = __floats2half2_rn(a, b);
-    return *reinterpret_cast<uint32_t*>(&h);
-  }
-};
-
-// 2^x on the FMA pipe, to take part of the softmax's exponentials off the
-// 16-per-clock MUFU unit.  Range reduction n = round(x) by the 1.5 * 2^23
-// rounding trick (Cody-Waite), f = x - n in [-0.5, 0.5], 2^f by a degree-3
-// polynomial fitted here (iterated weighted least squares on 20001 points for
-// minimal relative error; max relative error 7.6e-5 with fp32 Horner
-// evaluation, against 3.9e-3 = the bf16 precision P is rounded to), and
-// 2^n added to the exponent field.  x is clamped at -126 so the exponent
-// field stays >= 0; callers only pass x <= 8 (lazy rescale) and never -inf.
-__device__ __forceinline__ float poly_exp2(float x) {
-  x = fmaxf(x, -126.0f);
-  const float kRound = 12582912.0f;  // 1.5 * 2^23
-  const float t = x + kRound;
-  const float n = t - kRound;
-  const float f = x - n;
-  const float p =
-      fmaf(fmaf(fmaf(0.05517556518316269f, f, 0.24262112379074097f), f, 0.6932611465454102f), f, 0.999927282333374f);
-  const int ni = __float_as_int(t) - __float_as_int(kRound);
-  return __int_as_float(__float_as_int(p) + (ni << 23));
-}
-
-// D[tmem] (+)= A[tmem] * B[smem], kind::f16.  A has M rows = TMEM lanes and K
-// packed two 16-bit values per 32-bit column (8 columns per K = 16 step).
-__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                            uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
-      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
-      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
-      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
-      : "memory");
-}
 
 template <typename T, int D, int STAGES>
 __global__ void __launch_bounds__(kAttnThreads, 1)
@@ -521,37 +446,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 }
 
 // ---------------------------------------------------------------- host side
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  if (fn == nullptr) {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(ptr);
-  }
-  return fn;
-}
-
-// 4-D map over [B, H, T, D] (dims innermost first: D, H, T, B), 128-byte swizzle,
-// box (64 dims, box_h heads, 64 tokens, 1).  Out-of-range boxes read zeros.
-static bool make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int B, int H, int T, int D,
-                     const int64_t* s, int box_h) {
-  EncodeTiledFn fn = encode_fn();
-  if (fn == nullptr) return false;
-  const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)B};
-  const cuuint64_t strides[3] = {(cuuint64_t)s[1] * 2, (cuuint64_t)s[2] * 2, (cuuint64_t)s[0] * 2};
-  const cuuint32_t box[4] = {64, (cuuint32_t)box_h, 64, 1};
-  const cuuint32_t estr[4] = {1, 1, 1, 1};
-  return fn(m, dt, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 template <typename T, int D, int STAGES>
 static cudaError_t launch_typed(const AttnArgs& a, CUtensorMapDataType dt, cudaStream_t stream) {
   using L = AttnLayout<D, STAGES>;
@@ -559,33 +453,9 @@ static cudaError_t launch_typed(const AttnArgs& a, CUtensorMapDataType dt, cudaS
   if (!make_map(&tmq, a.q, dt, a.B, a.Hq, a.T, D, a.qs, 2) || !make_map(&tmk, a.k, dt, a.B, a.Hkv, a.T, D, a.ks, 1) ||
       !make_map(&tmv, a.v, dt, a.B, a.Hkv, a.T, D, a.vs, 1))
     return cudaErrorInvalidValue;
-  AttnParams p;
-  p.idx = a.idx;
-  p.isb = a.is[0];
-  p.isg = a.is[1];
-  p.isq = a.is[2];
-  p.out = a.out;
-  p.osb = a.os[0];
-  p.osh = a.os[1];
-  p.ost = a.os[2];
-  p.Hq = a.Hq;
-  p.Hkv = a.Hkv;
-  p.T = a.T;
-  p.Kw = a.Kw;
-  p.qb = (a.T + 63) / 64;
-  p.q_begin = a.q_begin;
-  p.nq = a.q_end - a.q_begin;
-  p.rep = a.Hq / a.Hkv;
-  p.n_pair = (p.rep + 1) / 2;
-  p.n_cta = (p.n_pair + 1) / 2;
-  p.scale_log2 = a.scale * 1.4426950408889634f;
-  p.status = a.status;
-  // Output maps over the LOGICAL [B, Hq, T, D] output strides, one head per box.
+  const AttnParams p = attn_params(a);
   OutMaps om;
-  om.count = 1 + a.n_peer;
-  if (!make_map(&om.m[0], a.out, dt, a.B, a.Hq, a.T, D, a.os, 1)) return cudaErrorInvalidValue;
-  for (int pp = 0; pp < a.n_peer; ++pp)
-    if (!make_map(&om.m[1 + pp], a.peer_out[pp], dt, a.B, a.Hq, a.T, D, a.os, 1)) return cudaErrorInvalidValue;
+  if (!attn_out_maps(a, dt, D, &om)) return cudaErrorInvalidValue;
   const size_t smem = L::smem_bytes(a.Kw);
   auto kern = attn_fwd_sm100_kernel<T, D, STAGES>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -600,10 +470,22 @@ constexpr size_t kMaxSmem = 227 * 1024;
 
 int attn_sm100_max_kw(int D) {
   const size_t base = D == 128 ? AttnLayout<128, 4>::smem_bytes(0) : AttnLayout<64, 4>::smem_bytes(0);
-  return static_cast<int>((kMaxSmem - base) / 4);
+  const int single = static_cast<int>((kMaxSmem - base) / 4);
+  return std::min(single, attn_pair_max_kw(D));  // either kernel may run the call
+}
+
+// The pair kernel (attn_pair_sm100.cu) is the default; SPRUCE_ATTN_KERNEL=single
+// selects this one-block-per-step kernel (for comparison).
+static bool use_single_block_kernel() {
+  static const int single = [] {
+    const char* v = getenv("SPRUCE_ATTN_KERNEL");
+    return (v != nullptr && strcmp(v, "single") == 0) ? 1 : 0;
+  }();
+  return single != 0;
 }
 
 cudaError_t launch_attn_sm100(const AttnArgs& a, int dtype, cudaStream_t stream) {
+  if (!use_single_block_kernel()) return launch_attn_pair(a, dtype, stream);
   if (a.Kw > attn_sm100_max_kw(a.D)) return cudaErrorInvalidValue;
   if (dtype == SPRUCE_DTYPE_BF16) {
     if (a.D == 128) return launch_typed<__nv_bfloat16, 128, 4>(a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, stream);

@@ -67,6 +67,9 @@ cudaError_t launch_attn_sm100(const AttnArgs& a, int dtype, cudaStream_t stream)
 cudaError_t launch_attn_f32(const AttnArgs& a, cudaStream_t stream);
 // Largest row width the tcgen05 kernel accepts for this head dim.
 int attn_sm100_max_kw(int D);
+// Two selected blocks per step (N = 128 QK MMAs); attn_pair_sm100.cu.
+cudaError_t launch_attn_pair(const AttnArgs& a, int dtype, cudaStream_t stream);
+int attn_pair_max_kw(int D);
 
 // K/V summary table of the residual tree (summaries.cu).
 struct KvSummaryArgs {

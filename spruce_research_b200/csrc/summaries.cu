@@ -36,7 +36,6 @@
 namespace spruce {
 
 constexpr int kSumSeg = 16;       // smallest prefix segment (tokens); the workspace is sized for it
-constexpr int kSumUnroll = 16;    // rows loaded together by the segment kernel
 constexpr int kSumThreads = 256;  // segment and node kernels
 constexpr int kScanLanes = 8;     // columns per scan CTA
 constexpr int kScanRows = 128;    // rows of segments per scan CTA
