@@ -36,7 +36,12 @@ sys.path.insert(0, ROOT)
 
 METRIC = "sparse-prefill ms/layer & effective TFLOP/s at 128K, 10% density, 1/2/4/8 B200"
 PEAKS_FILE = os.path.join(ROOT, "MEASURED_PEAKS.json")
-TRAFFIC_FILE = os.path.join(ROOT, "profiles", "attn_fwd_sm100_c2.md")
+# The attention kernel the library runs (SPRUCE_ATTN_KERNEL=single selects the one-block-per-step kernel)
+# and the ncu summary that holds its DRAM bytes per full-size launch.
+ATTN_KERNEL = ("attn_fwd_sm100_kernel<bf16,128,4>" if os.environ.get("SPRUCE_ATTN_KERNEL") == "single"
+               else "attn_pair_sm100_kernel<bf16,128,2>")
+TRAFFIC_FILE = os.path.join(ROOT, "profiles", "attn_fwd_sm100_c2.md" if os.environ.get("SPRUCE_ATTN_KERNEL") == "single"
+                            else "attn_pair_sm100_c2.md")
 FALLBACK_PEAK_TFLOPS = 1590.0
 
 
@@ -392,7 +397,7 @@ def run_b200(args):
         "config": config_dict(args, shape, K, entries, world),
         "breakdown_ms": {"selector": sel_ms_max, "attention": attn_ms_max,
                          ("fence" if fused else "gather"): gather_ms_max},
-        "roofline": {"bound": "tensor", "kernel": "attn_fwd_sm100_kernel<bf16,128,4>",
+        "roofline": {"bound": "tensor", "kernel": ATTN_KERNEL,
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                      "peak_source": peak_src + ", of measured",
                      "flops_per_launch": r_flops, "traffic": profiled_traffic(shape.tokens)},
