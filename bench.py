@@ -9,6 +9,7 @@ the layer is sharded by KV group (N=2, 4) or half group (N=8) and the outputs
 are all-gathered over NCCL; total work is fixed, so scaling is strong.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+    python bench.py --sweep          # config 4: variable-length batch, densities 2..100%
 
 `value` is effective TFLOP/s of the selected tiles (algorithmic FLOPs of the
 step / device time of the step, max over ranks); `e2e` is the same metric
@@ -60,6 +61,8 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target length of one CPU sample")
     ap.add_argument("--gather", choices=("fused", "nccl"), default="fused",
                     help="N>1 output all-gather: NVLink peer stores in the attention epilogue, or NCCL")
+    ap.add_argument("--sweep", action="store_true",
+                    help="config 4 instead: 8 variable-length sequences, densities 2..100%%, one GPU")
     return ap.parse_args()
 
 
@@ -455,10 +458,92 @@ def run_reference(args):
     print(json.dumps(result), flush=True)
 
 
+def run_sweep(args):
+    """a packed batch of 8 sequences, lengths U[8192, 131072] rounded to 64,
+    28Q/4KV heads, d=128, bf16, at densities 2/5/10/25/50/100%; the 100% case is checked
+    against dense causal attention (torch's SDPA in bf16, a checker only)."""
+    import torch
+    import torch.nn.functional as F
+
+    from spruce_research_b200.synthetic import (LayerShape, causal_block_entries, k_for_density,
+                                                make_gate_weights, make_layer_inputs, sparse_attention_flops)
+    from spruce_research_b200.varlen import VarlenSparsePrefill
+
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator().manual_seed(args.seed + 4)
+    lengths = [int(x) // 64 * 64 for x in torch.randint(8192, 131072 + 1, (8,), generator=gen)]
+    Hq, Hkv, D = 28, 4, 128
+    qs, ks, vs = [], [], []
+    for n, T in enumerate(lengths):
+        q, k, v = make_layer_inputs(LayerShape(1, Hq, Hkv, T, D), torch.bfloat16, args.seed + 100 + n)
+        qs.append(q[0].transpose(0, 1))
+        ks.append(k[0].transpose(0, 1))
+        vs.append(v[0].transpose(0, 1))
+    q = torch.cat(qs).contiguous().to(dev)
+    k = torch.cat(ks).contiguous().to(dev)
+    v = torch.cat(vs).contiguous().to(dev)
+    del qs, ks, vs
+    cu = [0]
+    for T in lengths:
+        cu.append(cu[-1] + T)
+    wq, wk = make_gate_weights(1, D, D, args.seed + 1000, device=dev)
+    runner = VarlenSparsePrefill(wq[0], wk[0])
+    out = torch.empty_like(q)
+    peak, peak_src = measured_peak()
+    rows = []
+    for density in (0.02, 0.05, 0.10, 0.25, 0.50, 1.0):
+        flops = 0.0
+        for T in lengths:
+            qb = (T + 63) // 64
+            K = runner.k_for(T, density, None)
+            flops += sparse_attention_flops(LayerShape(1, Hq, Hkv, T, D), causal_block_entries(qb, K))
+        for _ in range(max(1, args.warmup)):
+            runner(q, k, v, cu, density=density, out=out)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            runner(q, k, v, cu, density=density, out=out)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        rows.append({"density": density, "ms_per_batch": ms, "tflops": flops / (ms * 1e-3) / 1e12,
+                     "frac_of_peak": flops / (ms * 1e-3) / 1e12 / peak,
+                     "k_selected": [runner.k_for(T, density, None) for T in lengths]})
+    # 100%: every causal block, which must equal dense causal attention
+    runner(q, k, v, cu, density=1.0, out=out)
+    worst_max, err_sum, n_el = 0.0, 0.0, 0
+    for a, b in zip(cu, cu[1:]):
+        dense = F.scaled_dot_product_attention(q[a:b].transpose(0, 1)[None], k[a:b].transpose(0, 1)[None],
+                                               v[a:b].transpose(0, 1)[None], is_causal=True,
+                                               enable_gqa=True)[0].transpose(0, 1)
+        err = (out[a:b].float() - dense.float()).abs()
+        worst_max = max(worst_max, err.max().item())
+        err_sum += err.sum().item()
+        n_el += err.numel()
+    ten = next(r for r in rows if r["density"] == 0.10)
+    result = {
+        "metric": "sparse-prefill density/length sweep (config 4), effective TFLOP/s",
+        "value": ten["tflops"], "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ten["ms_per_batch"], "higher_is_better": True, "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1) Q/K/V, RoPE base 1e6, planted affinity",
+        "config": {"workload": "config 4: packed batch of 8 sequences, 28Q/4KV heads, d=128, bf16",
+                   "lengths": lengths, "tokens": cu[-1]},
+        "peak": peak, "peak_source": peak_src,
+        "sweep": rows,
+        "dense_check": {"max_abs": worst_max, "mean_abs": err_sum / n_el,
+                        "pass": worst_max < 2e-2 and err_sum / n_el < 2e-3,
+                        "reference": "torch scaled_dot_product_attention (bf16, causal, GQA) per sequence"},
+    }
+    print(json.dumps(result), flush=True)
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.sweep:
+        run_sweep(args)
     else:
         run_b200(args)
 

@@ -96,3 +96,18 @@ def test_charged_density_counts_dense_layers_as_full_triangles():
     d = charged_route_density(sel, dense_layers=[1])
     assert d["maximum_causal_block_entries"] == 2 * 10
     assert d["charged_block_entries"] == (1 + 2 + 2 + 2) + 10
+
+
+def test_block_mask_launcher_checks_and_index_conversion():
+    from spruce_research_b200.kernels.seerattention import block_mask_to_indices, block_sparse_triton
+
+    mask = torch.zeros((1, 2, 3, 3), dtype=torch.bool)
+    mask[0, 0, 0, 0] = mask[0, 0, 2, 0] = mask[0, 0, 2, 2] = True
+    mask[0, 1, 1, 1] = mask[0, 1, 1, 2] = True        # a future column is ignored
+    ids = block_mask_to_indices(mask)
+    assert ids.dtype == torch.int32 and ids.shape == (1, 2, 3, 2)
+    assert ids[0, 0].tolist() == [[0, -1], [-1, -1], [0, 2]]
+    assert ids[0, 1].tolist() == [[-1, -1], [1, -1], [-1, -1]]
+    q = torch.zeros(1, 2, 130, 64)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        block_sparse_triton(q, q, q, mask, 0.1)

@@ -156,3 +156,22 @@ def test_gpu_validator_raises_reference_messages():
         with pytest.raises(AssertionError) as cpu_err:
             O.validate_selected_blocks(t.cpu())
         assert str(gpu_err.value) == str(cpu_err.value)
+
+
+@pytest.mark.parametrize("dtype,D", [(torch.bfloat16, 128), (torch.float16, 64)])
+def test_block_mask_launcher_matches_oracle_per_head_masks(dtype, D):
+    # kernels/seerattention_triton.py:71-90 of the reference: BHSD q/k/v with K/V
+    # expanded per head, a per-head bool block mask, output BHSD.
+    from spruce_research_b200.kernels.seerattention import block_mask_to_indices, block_sparse_triton
+
+    gen = torch.Generator().manual_seed(21)
+    B, H, T = 2, 3, 64 * 5 + 17
+    qb = (T + 63) // 64
+    q, k, v = (torch.randn((B, H, T, D), generator=gen).to(dtype) for _ in range(3))
+    mask = torch.rand((B, H, qb, qb), generator=gen) > 0.5
+    mask |= torch.eye(qb, dtype=torch.bool)  # every row keeps its diagonal block
+    out = block_sparse_triton(q.cuda(), k.cuda(), v.cuda(), mask.cuda(), D ** -0.5)
+    assert out.shape == (B, H, T, D) and out.dtype == dtype
+    want = O.sparse_attention(q, k, v, block_mask_to_indices(mask), out_dtype=torch.float32)  # [B, T, H, D]
+    err = (out.float().cpu().transpose(1, 2) - want).abs()
+    assert err.max().item() < 2e-2 and err.mean().item() < 2e-3
