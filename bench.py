@@ -46,6 +46,26 @@ TRAFFIC_FILE = os.path.join(ROOT, "profiles", "attn_fwd_sm100_c2.md" if os.envir
 FALLBACK_PEAK_TFLOPS = 1590.0
 
 
+# The one JSON line goes to the process's real stdout; everything else -- including what
+# native libraries (NCCL's version banner, for one) write to file descriptor 1 -- goes to
+# stderr, so rank 0's stdout carries exactly one line.
+_JSON_OUT = None
+
+
+def _claim_stdout():
+    global _JSON_OUT
+    if _JSON_OUT is None:
+        sys.stdout.flush()
+        _JSON_OUT = os.fdopen(os.dup(1), "w")
+        os.dup2(2, 1)
+
+
+def emit(result: dict) -> None:
+    out = _JSON_OUT if _JSON_OUT is not None else sys.stdout
+    out.write(json.dumps(result) + "\n")
+    out.flush()
+
+
 def parse_args():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -260,7 +280,8 @@ def run_b200(args):
     q, k, v = make_layer_inputs(shape, torch.bfloat16, args.seed, device=dev)
     wq, wk = make_gate_weights(1, shape.head_dim, shape.head_dim, args.seed + 1, device=dev)
     layer = SparsePrefillLayer(wq[0], wk[0], K, local_window=0, sink_blocks=1)
-    shard = plan(world, rank, shape.kv_heads, qb)
+    # the fused gather takes unequal chunks, so its half-group split balances selected tiles
+    shard = plan(world, rank, shape.kv_heads, qb, k_selected=K if args.gather == "fused" else None)
     runner = ShardedSparsePrefill(shard, layer)
     g0, g1 = shard.groups
     rep = shape.q_heads // shape.kv_heads
@@ -412,7 +433,7 @@ def run_b200(args):
     if cpu is not None:
         result["cpu_baseline"] = cpu
     if rank == 0:
-        print(json.dumps(result), flush=True)
+        emit(result)
     if world > 1:
         dist.barrier(device_ids=[local])
         if peer is not None:
@@ -455,7 +476,7 @@ def run_reference(args):
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "ms_per_step extrapolates the sample's rate to the whole layer",
     }
-    print(json.dumps(result), flush=True)
+    emit(result)
 
 
 def run_sweep(args):
@@ -535,11 +556,12 @@ def run_sweep(args):
                         "pass": worst_max < 2e-2 and err_sum / n_el < 2e-3,
                         "reference": "torch scaled_dot_product_attention (bf16, causal, GQA) per sequence"},
     }
-    print(json.dumps(result), flush=True)
+    emit(result)
 
 
 def main():
     args = parse_args()
+    _claim_stdout()
     if args.impl == "reference":
         run_reference(args)
     elif args.sweep:

@@ -37,7 +37,32 @@ class Shard:
     parts: int                  # ranks per group (1 = whole groups)
 
 
-def plan(world: int, rank: int, kv_heads: int, query_blocks: int) -> Shard:
+def balanced_cuts(query_blocks: int, parts: int, k_selected: int) -> list[int]:
+    """Query-block boundaries giving each part about the same selected tiles.
+
+    Row i holds min(i + 1, K) blocks, so equal row counts leave the later part
+    with more work (5.4% more in the second half at config 2).
+    """
+    work = [min(i + 1, k_selected) for i in range(query_blocks)]
+    total = sum(work)
+    cuts, acc, p = [0], 0, 1
+    for i, w in enumerate(work):
+        if p < parts and acc + w / 2 > total * p / parts:
+            cuts.append(i)
+            p += 1
+        acc += w
+    while len(cuts) < parts:
+        cuts.append(query_blocks)
+    return cuts + [query_blocks]
+
+
+def plan(world: int, rank: int, kv_heads: int, query_blocks: int, k_selected: int | None = None) -> Shard:
+    """This rank's KV groups and query-block range.
+
+    With ``k_selected`` the query blocks of a group are split by selected
+    tiles (:func:`balanced_cuts`) instead of into equal parts; only the fused
+    all-gather accepts such unequal chunks.
+    """
     if world < 1 or not 0 <= rank < world:
         raise ValueError(f"bad rank {rank} of world {world}")
     if world <= kv_heads:
@@ -48,9 +73,12 @@ def plan(world: int, rank: int, kv_heads: int, query_blocks: int) -> Shard:
     if world % kv_heads:
         raise ValueError(f"{world} GPUs is not a multiple of {kv_heads} KV groups")
     parts = world // kv_heads
+    g, p = divmod(rank, parts)
+    if k_selected is not None:
+        cuts = balanced_cuts(query_blocks, parts, k_selected)
+        return Shard(rank, world, (g, g + 1), (cuts[p], cuts[p + 1]), parts)
     if query_blocks % parts:
         raise ValueError(f"{query_blocks} query blocks do not split into {parts} equal parts")
-    g, p = divmod(rank, parts)
     chunk = query_blocks // parts
     return Shard(rank, world, (g, g + 1), (p * chunk, (p + 1) * chunk), parts)
 

@@ -97,3 +97,20 @@ def test_shard_plan_rejects_uneven_splits():
         plan(3, 0, 4, 2048)
     with pytest.raises(ValueError):
         plan(8, 0, 4, 2047)
+
+
+def test_balanced_split_equalises_selected_tiles():
+    from spruce_research_b200.sharding import balanced_cuts
+
+    qb, K = 2048, 106
+    cuts = balanced_cuts(qb, 2, K)
+    work = [min(i + 1, K) for i in range(qb)]
+    a, b = sum(work[:cuts[1]]), sum(work[cuts[1]:])
+    assert cuts[0] == 0 and cuts[-1] == qb and abs(a - b) <= K
+    assert sum(work[1024:]) / sum(work[:1024]) > 1.05        # the equal-rows split is 5% off
+    for world in (8, 16):
+        seen = torch.zeros(4, qb, dtype=torch.int32)
+        for r in range(world):
+            s = plan(world, r, 4, qb, k_selected=K)
+            seen[s.groups[0]:s.groups[1], s.q_blocks[0]:s.q_blocks[1]] += 1
+        assert torch.equal(seen, torch.ones_like(seen))
