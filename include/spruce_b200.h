@@ -65,11 +65,13 @@ SPRUCE_API int spruce_group_avg_tokens(const void *x, const int64_t x_strides[4]
                             int64_t T, int64_t D, int64_t G, void *out, void *stream);
 
 /*
- * _proto_pool_seq, teacher/chunked_extract.py:27-72, mean prototype (P = 1):
- * x [B, H, T, D] (strided) -> out [B, H, nb, 1, D] contiguous, nb =
- * ceil(T / block), block = 64.  Bit-exact with the reference's rounding points
- * (16-row fp32 partial sums, sum rounded to dtype, divided by the real row
- * count of the block).  P > 1 returns SPRUCE_ERR_UNSUPPORTED.
+ * _proto_pool_seq, teacher/chunked_extract.py:27-72:
+ * x [B, H, T, D] (strided) -> out [B, H, nb, P, D] contiguous, nb =
+ * ceil(T / block), block = 64.  Prototype 0 is the block mean, bit-exact with
+ * the reference's rounding points (16-row fp32 partial sums, sum rounded to
+ * dtype, divided by the real row count of the block); prototypes 1..P-1 are
+ * the rows farthest from it (fp32 squared L2, descending, ties to the lower
+ * row), the mean where a ragged block has no further row.  1 <= P <= 64.
  */
 SPRUCE_API int spruce_proto_pool(const void *x, const int64_t x_strides[4], int dtype, int64_t B, int64_t H, int64_t T,
                       int64_t D, int64_t block, int64_t P, void *out, void *stream);
@@ -86,6 +88,20 @@ SPRUCE_API int spruce_pool_qk(const void *q, const int64_t q_strides[4], const v
                    void *pooled_k, void *stream);
 
 /*
+ * The selector's prototype features with P prototypes per block
+ * (teacher/chunked_extract.py:27-72 on _group_avg_tokens(q) and on k):
+ * prototype 0 is the block mean (exactly as spruce_pool_qk), prototypes
+ * 1..P-1 are the block's rows farthest (fp32 squared L2) from that mean, in
+ * descending distance, ties to the lower row; slots a ragged last block cannot
+ * fill repeat the mean.  pooled_q / pooled_k [B, Hkv, ceil(T/64), P, D]
+ * contiguous in the input dtype.  1 <= P <= 64 (spruce_proto_pool takes the
+ * same P for one tensor).
+ */
+SPRUCE_API int spruce_pool_qk_protos(const void *q, const int64_t q_strides[4], const void *k,
+                                     const int64_t k_strides[4], int dtype, int64_t B, int64_t Hq, int64_t Hkv,
+                                     int64_t T, int64_t D, int64_t P, void *pooled_q, void *pooled_k, void *stream);
+
+/*
  * FlatGate projection, selector/gate.py:120-127 (project_queries /
  * project_keys) and :47-48: out[n, :] = fp32(x[n, :]) @ W, x [N, D] contiguous
  * in dtype, W [D, P] fp32 contiguous, out [N, P] fp32.  Fixed fma order over D.
@@ -100,6 +116,19 @@ SPRUCE_API int spruce_gate_project(const void *x, int dtype, int64_t N, int64_t 
  */
 SPRUCE_API int spruce_gate_scores(const float *qp, const float *kp, int64_t R, int64_t qb, int64_t kb, int64_t P,
                        float *out, void *stream);
+
+/*
+ * MaxSim gate scores (selector/gate.py:29-101 forward, :104-117 and
+ * :132-171 candidate scoring): qp [R, nq, P, pdim], kp [R, nk, P, pdim] fp32
+ * projected prototypes (spruce_gate_project of each prototype row);
+ *   out[r, q, c] = max over (i, j) of qp[r,q,i,:] . kp[r,key,j,:] / sqrt(pdim)
+ * with key = c for every c < nk (ids == NULL, ncols == nk: the full score
+ * matrix) or key = ids[r, q, c] clamped to [0, nk) (int64 candidate node ids,
+ * ncols per row).  Each dot is one fp32 fma chain in index order; with P = 1
+ * the result equals spruce_gate_scores.  1 <= P <= 8.  out fp32 [R, nq, ncols].
+ */
+SPRUCE_API int spruce_gate_maxsim(const float *qp, const float *kp, const int64_t *ids, int64_t R, int64_t nq,
+                                  int64_t nk, int64_t ncols, int64_t P, int64_t pdim, float *out, void *stream);
 
 /*
  * Fused flat-gate selection: scores (as spruce_gate_scores), causal /

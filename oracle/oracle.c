@@ -486,6 +486,44 @@ void oracle_kv_summary_table(const void *key, const void *value, int dtype, cons
     }
 }
 
+/*
+ * MaxSim gate scores, selector/gate.py:29-101 (forward) and :132-171
+ * (candidate scoring): out[r, q, c] = max over (i, j) of
+ * qp[r,q,i,:] . kp[r,key,j,:] / sqrt(pdim), key = c or ids[r,q,c] clamped to
+ * [0, nk).  The reference takes the dots as einsum / matmul reductions; here
+ * each dot is one fmaf chain in index order (the fixed order of the CUDA
+ * kernel), so the two agree bit for bit and sit within fp32 rounding of the
+ * reference.
+ */
+void oracle_maxsim(const float *qp, const float *kp, const int64_t *ids, int64_t R, int64_t nq, int64_t nk,
+                   int64_t ncols, int64_t P, int64_t pdim, float *out) {
+    const float denom = (float)sqrt((double)pdim);
+#ifdef _OPENMP
+#pragma omp parallel for collapse(2) schedule(static)
+#endif
+    for (int64_t r = 0; r < R; ++r) {
+        for (int64_t q = 0; q < nq; ++q) {
+            const float *qrow = qp + (r * nq + q) * P * pdim;
+            for (int64_t c = 0; c < ncols; ++c) {
+                int64_t key = c;
+                if (ids) {
+                    key = ids[(r * nq + q) * ncols + c];
+                    key = key < 0 ? 0 : (key >= nk ? nk - 1 : key);
+                }
+                const float *krow = kp + (r * nk + key) * P * pdim;
+                float best = -INFINITY;
+                for (int64_t i = 0; i < P; ++i)
+                    for (int64_t j = 0; j < P; ++j) {
+                        float acc = 0.0f;
+                        for (int64_t x = 0; x < pdim; ++x) acc = fmaf(qrow[i * pdim + x], krow[j * pdim + x], acc);
+                        if (acc > best) best = acc;
+                    }
+                out[(r * nq + q) * ncols + c] = best / denom;
+            }
+        }
+    }
+}
+
 /* Number of threads the OpenMP runtime will use (for the CPU-baseline report). */
 int oracle_num_threads(void) {
 #ifdef _OPENMP

@@ -14,6 +14,8 @@ reference's sparse-prefill path end to end:
   sparse attention       sparse/attention.py:143-274
   residual tree layout   interfaces/residual_summaries.py:73-122
   K/V summary table      sparse/summaries.py:29-142
+  outlier prototypes     teacher/chunked_extract.py:47-72
+  MaxSim gate scores     selector/gate.py:29-101, :132-171
 
 Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs import
 this module; the product path never does.  Parity is pinned by the golden
@@ -65,6 +67,7 @@ def lib():
         L.oracle_sparse_attention_rows.argtypes = [P, P, P, P, I64, I64, I64, I64, I64, I64, I64, F, I64, I64, P]
         L.oracle_kv_summary_table.argtypes = [P, P, ctypes.c_int, P, I64, I64, I64, I64, I64, I64, P, P, I64,
                                               P, P, P, P, P, P]
+        L.oracle_maxsim.argtypes = [P, P, P, I64, I64, I64, I64, I64, I64, P]
         L.oracle_num_threads.restype = ctypes.c_int
         _lib = L
     return _lib
@@ -110,10 +113,34 @@ def block_mean(x: torch.Tensor, block: int = 64) -> torch.Tensor:
 
 
 def proto_pool_seq(x: torch.Tensor, block: int, P: int) -> torch.Tensor:
-    """[b, H, L, d] -> [b, H, nb, P, d] for P = 1 (the mean prototype)."""
-    if P != 1:
-        raise NotImplementedError("the oracle restates the P=1 (mean) prototype only")
-    return block_mean(x, block)[:, :, :, None, :]
+    """[b, H, L, d] -> [b, H, nb, P, d] (teacher/chunked_extract.py:27-72).
+
+    Prototype 0 is the block mean (oracle_block_mean, bit-exact).  For P > 1
+    the next P-1 are the block's real rows with the largest fp32 squared L2
+    distance to that mean (:53-57), in descending order with ties to the lower
+    row (torch.topk leaves tie order open); slots a ragged block cannot fill
+    repeat the mean (:62-72).
+    """
+    mean = block_mean(x, block)                       # [b, H, nb, d] in x's dtype
+    if P == 1:
+        return mean[:, :, :, None, :]
+    b, H, T, d = x.shape
+    nb = mean.shape[2]
+    xs = x.detach().cpu()
+    out = mean[:, :, :, None, :].repeat(1, 1, 1, P, 1)
+    m32 = mean.float().numpy()
+    x32 = xs.float().numpy()
+    for i in range(nb):
+        r0, r1 = i * block, min((i + 1) * block, T)
+        rows = x32[:, :, r0:r1, :]                    # [b, H, n, d]
+        diff = (rows - m32[:, :, i, None, :]).astype(np.float32)
+        dist = (diff * diff).sum(axis=-1, dtype=np.float32)     # [b, H, n]
+        for bb in range(b):
+            for h in range(H):
+                order = np.lexsort((np.arange(r1 - r0), -dist[bb, h]))   # descending, lower row first
+                for s, r in enumerate(order[:min(P - 1, block)]):
+                    out[bb, h, i, s + 1] = xs[bb, h, r0 + int(r)]
+    return out
 
 
 def project(x: torch.Tensor, W: torch.Tensor) -> torch.Tensor:
@@ -302,4 +329,18 @@ def kv_summary_table(key: torch.Tensor, value: torch.Tensor, starts, ends, block
                                   B, H, T, D, block_size, P, _ptr(st), _ptr(en), nodes,
                                   *(_ptr(out[n]) for n in ("keys", "values", "counts", "log_counts",
                                                            "range_starts", "range_ends")))
+    return out
+
+
+def maxsim(qp: torch.Tensor, kp: torch.Tensor, ids: torch.Tensor | None = None) -> torch.Tensor:
+    """MaxSim scores of fp32 projections qp [R, nq, P, p], kp [R, nk, P, p]; every key
+    column, or the candidate key ids [R, nq, C] (selector/gate.py:29-101, :132-171)."""
+    R, nq, P, p = qp.shape
+    nk = kp.shape[1]
+    qc = qp.detach().cpu().float().contiguous()
+    kc = kp.detach().cpu().float().contiguous()
+    idc = None if ids is None else ids.detach().cpu().to(torch.int64).contiguous()
+    ncols = nk if idc is None else idc.shape[2]
+    out = torch.empty((R, nq, ncols), dtype=torch.float32)
+    lib().oracle_maxsim(_ptr(qc), _ptr(kc), None if idc is None else _ptr(idc), R, nq, nk, ncols, P, p, _ptr(out))
     return out

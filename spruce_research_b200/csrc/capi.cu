@@ -93,11 +93,14 @@ static int pool_jobs(spruce::PoolJob j0, spruce::PoolJob j1, int njobs, int dtyp
 // query-block range of the selector reads); shapes already checked.
 static int pool_qk_range(const void* q, const int64_t q_strides[4], const void* k, const int64_t k_strides[4],
                          int dtype, int64_t B, int64_t Hq, int64_t Hkv, int64_t T, int64_t D, void* pooled_q,
-                         void* pooled_k, int q0, int q1, int k1, void* stream) {
-  spruce::PoolJob jq{q, q_strides[0], q_strides[1], q_strides[2], pooled_q, (int)(Hq / Hkv), (int)Hkv, q0, q1 - q0};
-  spruce::PoolJob jk{k, k_strides[0], k_strides[1], k_strides[2], pooled_k, 1, (int)Hkv, 0, k1};
+                         void* pooled_k, int q0, int q1, int k1, void* stream, int protos = 1) {
+  spruce::PoolJob jq{q, q_strides[0], q_strides[1], q_strides[2], pooled_q, (int)(Hq / Hkv), (int)Hkv, q0, q1 - q0,
+                     protos};
+  spruce::PoolJob jk{k, k_strides[0], k_strides[1], k_strides[2], pooled_k, 1, (int)Hkv, 0, k1, protos};
   return pool_jobs(jq, jk, 2, dtype, B, T, D, stream);
 }
+
+static constexpr int64_t kMaxProtos = SPRUCE_BLOCK;  // the mean plus at most every row of the block
 
 static int pool_jobs(spruce::PoolJob j0, spruce::PoolJob j1, int njobs, int dtype, int64_t B, int64_t T, int64_t D,
                      void* stream) {
@@ -114,14 +117,37 @@ int spruce_proto_pool(const void* x, const int64_t x_strides[4], int dtype, int6
                       int64_t D, int64_t block, int64_t P, void* out, void* stream) {
   if (!valid_dtype(dtype)) return fail(SPRUCE_ERR_INVALID, "unsupported dtype code %d", dtype);
   if (block != SPRUCE_BLOCK) return fail(SPRUCE_ERR_UNSUPPORTED, "block must be 64, got %lld", (long long)block);
-  if (P != 1) return fail(SPRUCE_ERR_UNSUPPORTED, "only the mean prototype (P=1) is implemented, got P=%lld", (long long)P);
+  if (P < 1) return fail(SPRUCE_ERR_INVALID, "P must be >= 1, got %lld", (long long)P);
+  if (P > kMaxProtos)
+    return fail(SPRUCE_ERR_UNSUPPORTED, "at most %lld prototypes per 64-token block, got P=%lld",
+                (long long)kMaxProtos, (long long)P);
   if (B < 0 || H < 1 || T < 0 || D < 1 || D > 256) return fail(SPRUCE_ERR_INVALID, "bad shape");
   if (!aligned16(x) || !aligned16(out) || !vec_strides_ok(x_strides, dtype, D))
     return fail(SPRUCE_ERR_UNSUPPORTED, "x must be 16-byte aligned with a unit last stride");
   if (B == 0 || T == 0) return SPRUCE_OK;
   const int nb = (int)((T + SPRUCE_BLOCK - 1) / SPRUCE_BLOCK);
-  spruce::PoolJob j{x, x_strides[0], x_strides[1], x_strides[2], out, 1, (int)H, 0, nb};
+  spruce::PoolJob j{x, x_strides[0], x_strides[1], x_strides[2], out, 1, (int)H, 0, nb, (int)P};
   return pool_jobs(j, j, 1, dtype, B, T, D, stream);
+}
+
+int spruce_pool_qk_protos(const void* q, const int64_t q_strides[4], const void* k, const int64_t k_strides[4],
+                          int dtype, int64_t B, int64_t Hq, int64_t Hkv, int64_t T, int64_t D, int64_t P,
+                          void* pooled_q, void* pooled_k, void* stream) {
+  if (!valid_dtype(dtype)) return fail(SPRUCE_ERR_INVALID, "unsupported dtype code %d", dtype);
+  if (B < 0 || Hq < 1 || Hkv < 1 || T < 0 || D < 1 || D > 256) return fail(SPRUCE_ERR_INVALID, "bad shape");
+  if (Hq % Hkv) return fail(SPRUCE_ERR_INVALID, "query heads (%lld) must be divisible by KV heads (%lld)",
+                            (long long)Hq, (long long)Hkv);
+  if (P < 1) return fail(SPRUCE_ERR_INVALID, "P must be >= 1, got %lld", (long long)P);
+  if (P > kMaxProtos)
+    return fail(SPRUCE_ERR_UNSUPPORTED, "at most %lld prototypes per 64-token block, got P=%lld",
+                (long long)kMaxProtos, (long long)P);
+  if (!aligned16(q) || !aligned16(k) || !aligned16(pooled_q) || !aligned16(pooled_k) ||
+      !vec_strides_ok(q_strides, dtype, D) || !vec_strides_ok(k_strides, dtype, D))
+    return fail(SPRUCE_ERR_UNSUPPORTED, "q/k must be 16-byte aligned with a unit last stride");
+  if (B == 0 || T == 0) return SPRUCE_OK;
+  const int nb = (int)((T + SPRUCE_BLOCK - 1) / SPRUCE_BLOCK);
+  return pool_qk_range(q, q_strides, k, k_strides, dtype, B, Hq, Hkv, T, D, pooled_q, pooled_k, 0, nb, nb, stream,
+                       (int)P);
 }
 
 int spruce_pool_qk(const void* q, const int64_t q_strides[4], const void* k, const int64_t k_strides[4], int dtype,
@@ -150,6 +176,20 @@ int spruce_gate_project(const void* x, int dtype, int64_t N, int64_t D, const fl
     default: e = spruce::launch_project<__half>(x, N, D, W, P, out, as_stream(stream)); break;
   }
   return cuda_status(e, "projection launch");
+}
+
+int spruce_gate_maxsim(const float* qp, const float* kp, const int64_t* ids, int64_t R, int64_t nq, int64_t nk,
+                       int64_t ncols, int64_t P, int64_t pdim, float* out, void* stream) {
+  if (R < 0 || nq < 0 || nk < 1 || ncols < 0 || pdim < 1 || pdim > 4096)
+    return fail(SPRUCE_ERR_INVALID, "bad MaxSim shape");
+  if (P < 1 || P > 8) return fail(SPRUCE_ERR_UNSUPPORTED, "MaxSim takes 1 to 8 prototypes, got %lld", (long long)P);
+  if (ids == nullptr && ncols != nk)
+    return fail(SPRUCE_ERR_INVALID, "without candidate ids every key is a column (ncols == nk)");
+  if (R * nq > INT32_MAX || nq > INT32_MAX || nk > INT32_MAX || ncols > INT32_MAX)
+    return fail(SPRUCE_ERR_UNSUPPORTED, "MaxSim shape too large");
+  return cuda_status(spruce::launch_maxsim(qp, kp, ids, R, (int)nq, (int)nk, (int)ncols, (int)P, (int)pdim, out,
+                                           as_stream(stream)),
+                     "maxsim launch");
 }
 
 int spruce_gate_scores(const float* qp, const float* kp, int64_t R, int64_t qb, int64_t kb, int64_t P, float* out,

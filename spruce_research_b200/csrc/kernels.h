@@ -9,10 +9,11 @@ namespace spruce {
 struct PoolJob {
   const void* x;       // [B, H, T, D] strided
   int64_t sb, sh, st;  // element strides (d stride is 1)
-  void* out;           // [B, Hout, nb, D] contiguous
+  void* out;           // [B, Hout, nb, protos, D] contiguous
   int rep;             // heads averaged per output row (1 = plain pooling)
   int hout;            // output heads
   int blk0, nblk;      // 64-token blocks [blk0, blk0 + nblk) are pooled
+  int protos = 1;      // prototypes per block: the mean, then the protos-1 rows farthest from it
 };
 
 template <typename T>
@@ -27,6 +28,10 @@ template <typename T>
 cudaError_t launch_project_rows(const void* x, int64_t groups, int qb, int row0, int nrows, int D, const float* W,
                                 int P, float* out, cudaStream_t stream);
 
+// MaxSim scores (P prototypes of dimension pdim per row / key): every column
+// (ids == null, ncols == nk) or the candidate key ids[r, q, c].
+cudaError_t launch_maxsim(const float* qp, const float* kp, const int64_t* ids, int64_t R, int nq, int nk, int ncols,
+                          int P, int pdim, float* out, cudaStream_t stream);
 cudaError_t launch_scores(const float* qp, const float* kp, int64_t R, int qb, int kb, int P, float* out,
                           cudaStream_t stream);
 int select_rows_for(int qb, int P, int64_t tiles16 = -1);

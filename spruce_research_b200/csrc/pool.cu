@@ -41,6 +41,8 @@ __global__ void __launch_bounds__(kPoolThreads) pool_block_kernel(PoolJob j0, Po
   extern __shared__ float pool_smem[];
   float* rows = pool_smem;                 // [64][D] group-averaged, already rounded to T
   float* part = pool_smem + kPoolBlock * D; // [4][D] 16-row partial sums
+  float* meanv = part + 4 * D;              // [D] the mean prototype (rounded to T), protos > 1
+  float* dist = meanv + D;                  // [64] squared distances to the mean, protos > 1
 
   int y = blockIdx.y;
   const PoolJob& job = (njobs > 1 && y >= j0.hout) ? j1 : j0;
@@ -89,13 +91,70 @@ __global__ void __launch_bounds__(kPoolThreads) pool_block_kernel(PoolJob j0, Po
   __syncthreads();
 
   // Phase 3: chunk totals in order, round, divide by the real row count, round.
-  T* out = static_cast<T*>(job.out) + ((int64_t)(b * job.hout + y) * nb + i) * D;
+  const int P = job.protos;
+  T* out = static_cast<T*>(job.out) + ((int64_t)(b * job.hout + y) * nb + i) * P * D;
   for (int d = threadIdx.x; d < D; d += kPoolThreads) {
     float total = 0.0f;
 #pragma unroll
     for (int c = 0; c < 4; ++c) total = __fadd_rn(total, part[c * D + d]);
     const float s = round_through<T>(total);
-    out[d] = Elem<T>::from_f(__fdiv_rn(s, static_cast<float>(count)));
+    const T m = Elem<T>::from_f(__fdiv_rn(s, static_cast<float>(count)));
+    out[d] = m;
+    meanv[d] = Elem<T>::to_f(m);
+  }
+  if (P == 1) return;  // uniform per CTA
+  __syncthreads();
+
+  // Phase 4 (teacher/chunked_extract.py:53-54): squared L2 distance of each real
+  // row to the mean, in fp32, one warp per row; pad rows of a ragged tail are -inf.
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int r = warp; r < kPoolBlock; r += kPoolThreads / 32) {
+    float acc = 0.0f;
+    for (int d = lane; d < D; d += 32) {
+      const float diff = __fsub_rn(rows[r * D + d], meanv[d]);
+      acc = __fadd_rn(acc, __fmul_rn(diff, diff));  // squares rounded, as pow(2) then sum
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (lane == 0) dist[r] = r < count ? acc : -INFINITY;
+  }
+  __syncthreads();
+
+  // Phase 5 (:55-57): the P-1 largest distances in descending order (ties to the
+  // lower row), by one warp: each of the 64 rows is held by lane r % 32.
+  __shared__ int pick[kPoolBlock];
+  if (warp == 0) {
+    float d0 = dist[lane], d1 = dist[lane + 32];
+    for (int s = 0; s < P - 1 && s < kPoolBlock; ++s) {
+      float best = d0;
+      int bi = lane;
+      if (d1 > best) {
+        best = d1;
+        bi = lane + 32;
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        if (ob > best || (ob == best && oi < bi)) {
+          best = ob;
+          bi = oi;
+        }
+      }
+      if (lane == 0) pick[s] = (best == -INFINITY) ? -1 : bi;  // only pad rows left: the mean (:62-67)
+      // a picked row drops out like a pad row (real distances are >= 0)
+      if (bi == lane) d0 = -INFINITY;
+      if (bi == lane + 32) d1 = -INFINITY;
+    }
+  }
+  __syncthreads();
+
+  // Phase 6 (:68-72): prototypes 1.. are the picked rows (exact copies), or the
+  // mean where the block has no further real row.
+  for (int e = threadIdx.x; e < (P - 1) * D; e += kPoolThreads) {
+    const int s = e / D, d = e % D;
+    const int r = s < kPoolBlock ? pick[s] : -1;
+    out[(int64_t)(s + 1) * D + d] = Elem<T>::from_f(r >= 0 ? rows[r * D + d] : meanv[d]);
   }
 }
 
@@ -135,7 +194,7 @@ __global__ void __launch_bounds__(256) group_avg_kernel(const T* x, int64_t sb, 
 template <typename T>
 cudaError_t launch_pool(PoolJob j0, PoolJob j1, int njobs, int B, int T_len, int D, cudaStream_t stream) {
   const int nb = (T_len + kPoolBlock - 1) / kPoolBlock;
-  const size_t smem = sizeof(float) * (kPoolBlock * D + 4 * D);
+  const size_t smem = sizeof(float) * (kPoolBlock * D + 4 * D + D + kPoolBlock);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(pool_block_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);

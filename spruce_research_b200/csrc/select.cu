@@ -737,3 +737,66 @@ cudaError_t launch_validate(const int32_t* sel, int64_t rows, int qb, int K, int
 }
 
 }  // namespace spruce
+
+// ------------------------------------------------------------------ MaxSim scores
+namespace spruce {
+
+// MaxSim gate scores (selector/gate.py:29-101, :104-117, :132-171):
+//   s[r, q, c] = max over (i, j) of qp[r, q, i, :] . kp[r, key(c), j, :] / denom
+// with key(c) = c (every key column) or ids[r, q, c] clamped to [0, nk) (the
+// candidate nodes of a tree level).  Every dot is one fma chain over p in
+// order, the max is exact in any order.  One CTA per (r, q): the row's P
+// query prototypes are staged in shared memory, each thread scores columns
+// c = tid, tid + 128, ... with P accumulators (one per key prototype) per
+// query prototype.
+template <int PMAX>
+__global__ void __launch_bounds__(128) maxsim_kernel(const float* __restrict__ qp, const float* __restrict__ kp,
+                                                     const int64_t* __restrict__ ids, int nq, int nk, int ncols,
+                                                     int P, int pdim, float denom, float* __restrict__ out) {
+  extern __shared__ float qsm[];  // [P][pdim]
+  const int64_t rq = blockIdx.x;  // r * nq + q
+  const int64_t r = rq / nq;
+  for (int e = threadIdx.x; e < P * pdim; e += 128) qsm[e] = qp[rq * P * pdim + e];
+  __syncthreads();
+  for (int c = threadIdx.x; c < ncols; c += 128) {
+    int64_t key = c;
+    if (ids != nullptr) {
+      key = ids[rq * ncols + c];
+      key = key < 0 ? 0 : (key >= nk ? nk - 1 : key);
+    }
+    const float* kr = kp + (r * nk + key) * P * pdim;
+    float best = -INFINITY;
+    for (int i = 0; i < P; ++i) {
+      const float* qi = qsm + i * pdim;
+      float acc[PMAX];
+#pragma unroll
+      for (int j = 0; j < PMAX; ++j) acc[j] = 0.0f;
+      for (int x = 0; x < pdim; ++x) {
+        const float qv = qi[x];
+#pragma unroll
+        for (int j = 0; j < PMAX; ++j)
+          if (j < P) acc[j] = __fmaf_rn(qv, __ldg(kr + j * pdim + x), acc[j]);
+      }
+#pragma unroll
+      for (int j = 0; j < PMAX; ++j)
+        if (j < P) best = fmaxf(best, acc[j]);
+    }
+    out[rq * ncols + c] = __fdiv_rn(best, denom);
+  }
+}
+
+cudaError_t launch_maxsim(const float* qp, const float* kp, const int64_t* ids, int64_t R, int nq, int nk, int ncols,
+                          int P, int pdim, float* out, cudaStream_t stream) {
+  if (R * nq == 0 || ncols == 0) return cudaSuccess;
+  const float denom = static_cast<float>(std::sqrt(static_cast<double>(pdim)));
+  const size_t smem = sizeof(float) * (size_t)P * pdim;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(maxsim_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  if (P > 8) return cudaErrorInvalidValue;
+  maxsim_kernel<8><<<(unsigned)(R * nq), 128, smem, stream>>>(qp, kp, ids, nq, nk, ncols, P, pdim, denom, out);
+  return cudaGetLastError();
+}
+
+}  // namespace spruce

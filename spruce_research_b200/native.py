@@ -61,8 +61,9 @@ def proto_pool(x: torch.Tensor, block: int = BLOCK, P: int = 1) -> torch.Tensor:
     return out
 
 
-def pool_qk(q: torch.Tensor, k: torch.Tensor):
-    """Selector inputs: (pooled_q, pooled_k), each [B, Hkv, qb, d] in the input dtype."""
+def pool_qk(q: torch.Tensor, k: torch.Tensor, P: int = 1):
+    """Selector inputs: (pooled_q, pooled_k), each [B, Hkv, qb, d] (P = 1) or
+    [B, Hkv, qb, P, d] (P prototypes: the mean and the P-1 farthest rows)."""
     _lib.require_cuda(q, k)
     B, Hq, T, d = q.shape
     Hkv = k.shape[1]
@@ -70,11 +71,16 @@ def pool_qk(q: torch.Tensor, k: torch.Tensor):
         raise ValueError("q and k must share a dtype")
     q, k = _vec_ok(q), _vec_ok(k)
     qb = (T + BLOCK - 1) // BLOCK
-    pq = torch.empty((B, Hkv, qb, d), device=q.device, dtype=q.dtype)
-    pk = torch.empty((B, Hkv, qb, d), device=q.device, dtype=q.dtype)
+    shape = (B, Hkv, qb, d) if P == 1 else (B, Hkv, qb, P, d)
+    pq = torch.empty(shape, device=q.device, dtype=q.dtype)
+    pk = torch.empty(shape, device=q.device, dtype=q.dtype)
     L = _lib.load()
-    _lib.check(L.spruce_pool_qk(q.data_ptr(), _lib.strides(q), k.data_ptr(), _lib.strides(k), _dt(q), B, Hq, Hkv, T,
-                                d, pq.data_ptr(), pk.data_ptr(), _lib.stream_of(q)))
+    if P == 1:
+        _lib.check(L.spruce_pool_qk(q.data_ptr(), _lib.strides(q), k.data_ptr(), _lib.strides(k), _dt(q), B, Hq, Hkv,
+                                    T, d, pq.data_ptr(), pk.data_ptr(), _lib.stream_of(q)))
+    else:
+        _lib.check(L.spruce_pool_qk_protos(q.data_ptr(), _lib.strides(q), k.data_ptr(), _lib.strides(k), _dt(q), B,
+                                           Hq, Hkv, T, d, P, pq.data_ptr(), pk.data_ptr(), _lib.stream_of(q)))
     return pq, pk
 
 
@@ -91,6 +97,29 @@ def gate_project(x: torch.Tensor, W: torch.Tensor) -> torch.Tensor:
     L = _lib.load()
     _lib.check(L.spruce_gate_project(xc.data_ptr(), _dt(xc), N, d, Wc.data_ptr(), p, out.data_ptr(),
                                      _lib.stream_of(x)))
+    return out
+
+
+def gate_maxsim(qp: torch.Tensor, kp: torch.Tensor, ids: torch.Tensor | None = None) -> torch.Tensor:
+    """MaxSim scores: qp [R, nq, P, p], kp [R, nk, P, p] fp32 -> [R, nq, nk] (every key)
+    or, with int64 candidate ids [R, nq, C], [R, nq, C] (selector/gate.py:29-101, :132-171)."""
+    _lib.require_cuda(qp, kp)
+    if qp.dtype != torch.float32 or kp.dtype != torch.float32:
+        raise ValueError("MaxSim takes fp32 projections")
+    R, nq, P, p = qp.shape
+    if kp.dim() != 4 or kp.shape[0] != R or kp.shape[2:] != (P, p):
+        raise ValueError(f"kp must be [{R}, nk, {P}, {p}], got {tuple(kp.shape)}")
+    nk = kp.shape[1]
+    qp, kp = qp.contiguous(), kp.contiguous()
+    if ids is not None:
+        _lib.require_cuda(ids)
+        if ids.dim() != 3 or tuple(ids.shape[:2]) != (R, nq):
+            raise ValueError(f"ids must be [{R}, {nq}, C], got {tuple(ids.shape)}")
+        ids = ids.to(torch.int64).contiguous()
+    ncols = nk if ids is None else ids.shape[2]
+    out = torch.empty((R, nq, ncols), device=qp.device, dtype=torch.float32)
+    _lib.check(_lib.load().spruce_gate_maxsim(qp.data_ptr(), kp.data_ptr(), None if ids is None else ids.data_ptr(),
+                                              R, nq, nk, ncols, P, p, out.data_ptr(), _lib.stream_of(qp)))
     return out
 
 

@@ -186,10 +186,36 @@ def summary_cases(ref):
     return cases
 
 
+def maxsim_cases(ref):
+    """The reference FlatGate (MaxSim, P = 8) on its own outlier-prototype features."""
+    gen = torch.Generator().manual_seed(13)
+    cases = {}
+    for n, (G, T, d, p, dt) in enumerate([(2, 64 * 12, 64, 64, torch.bfloat16), (1, 64 * 9 + 20, 128, 96, torch.float32)]):
+        q = torch.randn((1, G, T, d), generator=gen).to(dt)
+        k = torch.randn((1, G, T, d), generator=gen).to(dt)
+        q_feat = ref["proto_pool"](q, 64, 8)           # [1, G, nb, 8, d]
+        k_feat = ref["proto_pool"](k, 64, 8)
+        torch.manual_seed(100 + n)
+        gate = ref["FlatGate"](1, d, p).eval()
+        with torch.no_grad():
+            s = gate(q_feat.float(), k_feat.float())    # [1, G, nb, nb]
+            cand = torch.randint(0, q_feat.shape[2], (1, G, q_feat.shape[2], 5), generator=gen)
+            sc = gate.score_candidates(q_feat.float(), k_feat.float(), cand)
+        cases[f"ms{n}_q"] = _raw(q)
+        cases[f"ms{n}_k"] = _raw(k)
+        cases[f"ms{n}_dtype"] = np.array([{torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}[dt]])
+        cases[f"ms{n}_wq"] = gate.Wq.detach().numpy()
+        cases[f"ms{n}_wk"] = gate.Wk.detach().numpy()
+        cases[f"ms{n}_scores"] = s.numpy()
+        cases[f"ms{n}_cand"] = cand.numpy()
+        cases[f"ms{n}_cand_scores"] = sc.numpy()
+    return cases
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("SPRUCE_REFERENCE", "/root/reference"))
-    ap.add_argument("--only", choices=["all", "summaries"], default="all")
+    ap.add_argument("--only", choices=["all", "summaries", "maxsim"], default="all")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     from teacher.chunked_extract import _group_avg_tokens, _proto_pool_seq
@@ -207,6 +233,9 @@ def main():
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     if args.only == "summaries":
         np.savez_compressed(os.path.join(HERE, "summaries.npz"), **summary_cases(ref))
+        return
+    if args.only == "maxsim":
+        np.savez_compressed(os.path.join(HERE, "maxsim.npz"), **maxsim_cases(ref))
         return
 
     for name, (shape, dtype, seed, rope, K, lw, sink, keep_blocks) in CASES.items():
@@ -238,6 +267,7 @@ def main():
     np.savez_compressed(os.path.join(HERE, "packing.npz"), **packing_cases(ref))
     np.savez_compressed(os.path.join(HERE, "proto.npz"), **proto_cases(ref))
     np.savez_compressed(os.path.join(HERE, "summaries.npz"), **summary_cases(ref))
+    np.savez_compressed(os.path.join(HERE, "maxsim.npz"), **maxsim_cases(ref))
     print("wrote", sorted(f for f in os.listdir(HERE) if f.endswith(".npz")))
 
 

@@ -31,10 +31,24 @@ class GoldenCase:
     sink: int
     z: dict
 
-    def inputs(self, device="cpu"):
+    def matches_fixture(self) -> bool:
+        """True when this host regenerates the exact inputs the reference saw.
+
+        torch's CPU normal sampler has vector paths that depend on the host's
+        instruction set, so another CPU model can change the inputs' last bits.
+        The CPU suite (run where the fixtures were made) pins oracle == reference;
+        GPU tests compare CUDA == oracle on whatever inputs this host makes, and
+        also against the fixture outputs when this returns True.
+        """
         q, k, v = make_layer_inputs(self.shape, self.dtype, self.seed, rope_theta=self.rope)
         cs = np.array([q.double().sum().item(), k.double().sum().item(), v.double().sum().item()])
-        assert np.allclose(cs, self.z["checksum"], rtol=1e-12, atol=1e-6), "synthetic generator drifted"
+        return bool(np.allclose(cs, self.z["checksum"], rtol=1e-12, atol=1e-6))
+
+    def inputs(self, device="cpu", check=True):
+        q, k, v = make_layer_inputs(self.shape, self.dtype, self.seed, rope_theta=self.rope)
+        cs = np.array([q.double().sum().item(), k.double().sum().item(), v.double().sum().item()])
+        if check:
+            assert np.allclose(cs, self.z["checksum"], rtol=1e-12, atol=1e-6), "synthetic generator drifted"
         wq, wk = make_gate_weights(1, self.shape.head_dim, self.shape.head_dim, self.seed + 1000)
         if device != "cpu":
             # keep the reference's strided [B, H, T, D] views of token-major storage

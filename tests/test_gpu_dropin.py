@@ -97,16 +97,21 @@ def test_fp32_score_accumulation_keeps_fp16_overflow_finite():
 
 def test_flat_gate_scores_and_selection_match_reference():
     case = load_case("c1_8k")
-    q, k, v, wq, wk = case.inputs("cuda")
+    qc, kc, vc, wqc, wkc = case.inputs("cpu", check=False)
+    q, k, v, wq, wk = case.inputs("cuda", check=False)
+    ref = O.select_blocks(qc, kc, wqc, wkc, case.K, case.local_window, case.sink)
     pq, pk = pool_selector_features(q, k)
     gate = FlatGate(1, 128, 128).cuda().eval()
     with torch.no_grad():
         gate.Wq.copy_(wq[None])
         gate.Wk.copy_(wk[None])
     s = gate(pq[0][None], pk[0][None])
-    assert (s[0].cpu() - case.golden("scores")[0]).abs().max().item() < 1e-6
+    assert torch.equal(s[0].cpu(), ref["scores"][0])
     sel = gate.select_blocks(pq[0][None], pk[0][None], case.K, case.local_window, case.sink)
-    assert torch.equal(sel[0, 0].cpu(), case.golden("selected")[0])
+    assert torch.equal(sel[0, 0].cpu(), ref["selected"][0])
+    if case.matches_fixture():  # the reference's own outputs for these inputs
+        assert (s[0].cpu() - case.golden("scores")[0]).abs().max().item() < 1e-6
+        assert torch.equal(sel[0, 0].cpu(), case.golden("selected")[0])
 
 
 def test_proto_pool_and_group_average_match_reference():
@@ -115,10 +120,23 @@ def test_proto_pool_and_group_average_match_reference():
         dt = DT[int(z[f"proto{n}_dtype"][0])]
         x = from_raw(z[f"proto{n}_x"], dt).cuda()
         assert torch.equal(_proto_pool_seq(x, 64, 1).cpu(), from_raw(z[f"proto{n}_p1"], dt))
+        assert torch.equal(_proto_pool_seq(x, 64, 8).cpu(), from_raw(z[f"proto{n}_p8"], dt))
     x = torch.randn(1, 12, 70, 64, dtype=torch.bfloat16)
     assert torch.equal(_group_avg_tokens(x.cuda(), 2).cpu(), O.group_avg_tokens(x, 2))
-    with pytest.raises(ValueError, match="P=1"):
-        _proto_pool_seq(x.cuda(), 64, 8)
+    with pytest.raises(ValueError, match="at most 64 prototypes"):
+        _proto_pool_seq(x.cuda(), 64, 65)
+
+
+@pytest.mark.parametrize("P", [2, 4, 8])
+def test_outlier_prototypes_match_oracle_on_selector_features(P):
+    # the deployed selector's features: _proto_pool_seq(_group_avg_tokens(q)), _proto_pool_seq(k)
+    gen = torch.Generator().manual_seed(30 + P)
+    q = torch.randn((2, 28, 64 * 9 + 3, 128), generator=gen).to(torch.bfloat16)
+    k = torch.randn((2, 4, 64 * 9 + 3, 128), generator=gen).to(torch.bfloat16)
+    pq, pk = pool_selector_features(q.cuda(), k.cuda(), P)
+    assert pq.shape == (2, 4, 10, P, 128)
+    assert torch.equal(pq.cpu(), O.proto_pool_seq(O.group_avg_tokens(q, 4), 64, P))
+    assert torch.equal(pk.cpu(), O.proto_pool_seq(k, 64, P))
 
 
 def test_packing_drop_ins_match_reference_cases():
@@ -175,3 +193,27 @@ def test_block_mask_launcher_matches_oracle_per_head_masks(dtype, D):
     want = O.sparse_attention(q, k, v, block_mask_to_indices(mask), out_dtype=torch.float32)  # [B, T, H, D]
     err = (out.float().cpu().transpose(1, 2) - want).abs()
     assert err.max().item() < 2e-2 and err.mean().item() < 2e-3
+
+
+def test_maxsim_gate_matches_oracle_and_reference():
+    # FlatGate.forward / score_candidates with P = 8 (selector/gate.py:29-171)
+    from test_oracle_golden import _maxsim_case
+
+    z = load_npz("maxsim")
+    for n in range(2):
+        q, k, wq, wk = _maxsim_case(z, n)
+        qf, kf = _proto_pool_seq(q.cuda(), 64, 8), _proto_pool_seq(k.cuda(), 64, 8)   # [1, G, nb, 8, d]
+        gate = FlatGate(1, q.shape[-1], wq.shape[-1]).cuda().eval()
+        with torch.no_grad():
+            gate.Wq.copy_(wq)
+            gate.Wk.copy_(wk)
+        s = gate(qf, kf)[0].cpu()
+        qp, kp = O.project(qf[0].cpu(), wq[0]), O.project(kf[0].cpu(), wk[0])
+        assert torch.equal(s, O.maxsim(qp, kp))
+        want = torch.from_numpy(z[f"ms{n}_scores"])[0]
+        assert (s - want).abs().max().item() <= 2e-6 * want.abs().max().item()
+        cand = torch.from_numpy(z[f"ms{n}_cand"])
+        sc = gate.score_candidates(qf, kf, cand.cuda())[0].cpu()
+        assert torch.equal(sc, O.maxsim(qp, kp, cand[0]))
+    with pytest.raises(ValueError, match="1 to 8 prototypes"):
+        gate(torch.zeros(1, 1, 2, 9, q.shape[-1], device="cuda"), torch.zeros(1, 1, 2, 9, q.shape[-1], device="cuda"))

@@ -1,4 +1,9 @@
-"""CUDA path vs the reference's golden outputs and the CPU oracle (B200 only).
+"""CUDA path vs the CPU oracle and the reference's golden outputs (B200 only).
+
+The chain: the CPU suite pins oracle == reference on the fixtures' inputs;
+here CUDA == oracle on the inputs this host regenerates (torch's CPU sampler
+can differ in the last bit between CPU models), and CUDA == reference outputs
+directly whenever the regenerated inputs equal the fixture's.
 
 Parity bar:
   * pooled features, gate scores and selected block indices: bit-exact;
@@ -31,54 +36,63 @@ def assert_attention_close(actual: torch.Tensor, expected: torch.Tensor, dtype: 
         assert err.mean().item() <= ATOL_MEAN_16, f"{what}: mean-abs {err.mean().item():.3e}"
 
 
+def _case(name):
+    """(case, cpu inputs, cuda inputs, oracle selector result, inputs equal the fixture's)."""
+    case = load_case(name)
+    cpu = case.inputs("cpu", check=False)
+    cuda = case.inputs("cuda", check=False)
+    ref = O.select_blocks(cpu[0], cpu[1], cpu[3], cpu[4], case.K, case.local_window, case.sink)
+    return case, cpu, cuda, ref, case.matches_fixture()
+
+
 @pytest.mark.parametrize("name", CASE_NAMES)
 def test_pooling_bit_exact_with_reference(name):
-    case = load_case(name)
-    q, k, v, wq, wk = case.inputs("cuda")
+    case, cpu, (q, k, v, wq, wk), ref, same = _case(name)
     pq, pk = native.pool_qk(q, k)
     torch.cuda.synchronize()
-    assert torch.equal(pq.cpu(), case.golden("pooled_q")), "pooled Q differs from the reference"
-    assert torch.equal(pk.cpu(), case.golden("pooled_k")), "pooled K differs from the reference"
+    assert torch.equal(pq.cpu(), ref["pooled_q"]), "pooled Q differs from the oracle"
+    assert torch.equal(pk.cpu(), ref["pooled_k"]), "pooled K differs from the oracle"
+    if same:  # the oracle is pinned to these by the CPU suite; check directly too
+        assert torch.equal(pq.cpu(), case.golden("pooled_q")), "pooled Q differs from the reference"
+        assert torch.equal(pk.cpu(), case.golden("pooled_k")), "pooled K differs from the reference"
 
 
 @pytest.mark.parametrize("name", CASE_NAMES)
 def test_scores_bit_exact_with_oracle(name):
-    case = load_case(name)
-    q, k, v, wq, wk = case.inputs("cuda")
+    case, cpu, (q, k, v, wq, wk), ref, same = _case(name)
     pq, pk = native.pool_qk(q, k)
     qp = native.gate_project(pq, wq)
     kp = native.gate_project(pk, wk)
     B, G = pq.shape[:2]
     s = native.gate_scores(qp.flatten(0, 1), kp.flatten(0, 1)).view(B, G, pq.shape[2], pk.shape[2])
-    ref = O.select_blocks(*case.inputs("cpu")[:2], wq.cpu(), wk.cpu(), case.K, case.local_window, case.sink)
     assert torch.equal(qp.cpu(), ref["qp"]), "projection differs from the oracle's fixed fma order"
     assert torch.equal(kp.cpu(), ref["kp"])
     assert torch.equal(s.cpu(), ref["scores"]), "scores differ from the oracle"
-    # and within fp32 round-off of the reference's MKL scores
-    assert (s.cpu() - case.golden("scores")).abs().max().item() < 1e-6
+    if same:  # and within fp32 round-off of the reference's MKL scores
+        assert (s.cpu() - case.golden("scores")).abs().max().item() < 1e-6
 
 
 @pytest.mark.parametrize("name", CASE_NAMES)
 def test_selected_blocks_bit_exact_with_reference(name):
-    case = load_case(name)
-    q, k, v, wq, wk = case.inputs("cuda")
+    case, cpu, (q, k, v, wq, wk), ref, same = _case(name)
     sel = native.select_blocks(q, k, wq, wk, case.K, case.local_window, case.sink)
     torch.cuda.synchronize()
-    assert torch.equal(sel.cpu(), case.golden("selected")), "selected_blocks differ from the reference"
+    assert torch.equal(sel.cpu(), ref["selected"]), "selected_blocks differ from the oracle"
+    if same:
+        assert torch.equal(sel.cpu(), case.golden("selected")), "selected_blocks differ from the reference"
 
 
 @pytest.mark.parametrize("name", CASE_NAMES)
 def test_attention_matches_reference(name):
-    case = load_case(name)
-    q, k, v, wq, wk = case.inputs("cuda")
-    idx = case.golden("selected").cuda()
-    out = native.sparse_attention(q, k, v, idx)
+    case, cpu, (q, k, v, wq, wk), ref, same = _case(name)
+    idx = ref["selected"]
+    out = native.sparse_attention(q, k, v, idx.cuda())
     torch.cuda.synchronize()
-    rows = case.out_rows()
-    assert_attention_close(out[:, rows], case.golden("out"), case.dtype, name)
     # whole output against the oracle (fp32 math, same indices)
-    ref = O.sparse_attention(*case.inputs("cpu")[:3], case.golden("selected"), out_dtype=torch.float32)
-    assert_attention_close(out, ref, case.dtype, name + " vs oracle")
+    want = O.sparse_attention(cpu[0], cpu[1], cpu[2], idx, out_dtype=torch.float32)
+    assert_attention_close(out, want, case.dtype, name + " vs oracle")
+    if same:
+        assert_attention_close(out[:, case.out_rows()], case.golden("out"), case.dtype, name)
 
 
 ATTN_SHAPES = [

@@ -67,6 +67,15 @@ def test_mean_prototype_matches_reference():
         assert torch.equal(got, want), f"proto case {n}"
 
 
+def test_outlier_prototypes_match_reference():
+    # _proto_pool_seq(x, 64, 8): the mean plus the 7 rows farthest from it
+    z = load_npz("proto")
+    for n in range(3):
+        dt = DT[int(z[f"proto{n}_dtype"][0])]
+        x = from_raw(z[f"proto{n}_x"], dt)
+        assert torch.equal(O.proto_pool_seq(x, 64, 8), from_raw(z[f"proto{n}_p8"], dt)), f"proto case {n}"
+
+
 def test_validator_messages_follow_reference():
     def row(ids, k=4):
         return list(ids) + [-1] * (k - len(ids))
@@ -108,3 +117,28 @@ def test_golden_fixtures_are_small():
     total = sum(os.path.getsize(os.path.join(HERE, f)) for f in os.listdir(HERE) if f.endswith(".npz"))
     assert total < 6 * 2**20
     assert np.load(os.path.join(HERE, "c0.npz"))["selected"].dtype == np.int32
+
+
+def _maxsim_case(z, n):
+    dt = DT[int(z[f"ms{n}_dtype"][0])]
+    q, k = from_raw(z[f"ms{n}_q"], dt), from_raw(z[f"ms{n}_k"], dt)
+    wq, wk = torch.from_numpy(z[f"ms{n}_wq"]), torch.from_numpy(z[f"ms{n}_wk"])
+    return q, k, wq, wk
+
+
+def test_maxsim_scores_match_reference():
+    # FlatGate with P = 8 prototypes (selector/gate.py:29-101, :132-171) on the
+    # reference's own outlier features; MKL einsum vs fixed fma order: fp32 rounding.
+    z = load_npz("maxsim")
+    for n in range(2):
+        q, k, wq, wk = _maxsim_case(z, n)
+        qf, kf = O.proto_pool_seq(q, 64, 8)[0], O.proto_pool_seq(k, 64, 8)[0]       # [G, nb, 8, d]
+        qp, kp = O.project(qf, wq[0]), O.project(kf, wk[0])                         # [G, nb, 8, p]
+        want = torch.from_numpy(z[f"ms{n}_scores"])[0]
+        got = O.maxsim(qp, kp)
+        assert (got - want).abs().max().item() <= 2e-6 * want.abs().max().item()
+        cand = torch.from_numpy(z[f"ms{n}_cand"])[0]
+        got_c = O.maxsim(qp, kp, cand)
+        want_c = torch.from_numpy(z[f"ms{n}_cand_scores"])[0]
+        assert (got_c - want_c).abs().max().item() <= 2e-6 * want_c.abs().max().item()
+        assert torch.equal(got_c, torch.gather(got, 2, cand))
