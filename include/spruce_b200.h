@@ -131,6 +131,38 @@ SPRUCE_API int spruce_gate_maxsim(const float *qp, const float *kp, const int64_
                                   int64_t nk, int64_t ncols, int64_t P, int64_t pdim, float *out, void *stream);
 
 /*
+ * Key tree of the deployed selector (selector/tree.py:80-145): one level up.
+ * child [R, nchild, P, d] in dtype -> parent [R, ceil(nchild / radix), P, d]:
+ * prototype 0 = mean of the (up to radix) children's prototype 0, formed in
+ * dtype as the reference does; prototypes 1..P-1 = the children's prototypes
+ * farthest from it (distance in dtype), descending, ties to the lower
+ * candidate.  1 <= P <= 8, radix >= 2, radix * P <= 256.
+ */
+SPRUCE_API int spruce_tree_merge(const void *child, int dtype, int64_t R, int64_t nchild, int64_t P, int64_t d,
+                                 int64_t radix, void *parent, void *stream);
+
+/*
+ * One traversal level (scripts/eval_tree_traversal.py:83-108): the children
+ * of each row's selected nodes.  selected int64 [R, nq, S] (-1 = none),
+ * child_starts int64 [nchild] (first leaf block of each child) ->
+ * cand int64 [R, nq, S * radix] (ids to score: invalid ones clamped) and
+ * valid uint8 (parent selected, child exists, child starts at or before the
+ * row's block q).  S * radix <= 256.
+ */
+SPRUCE_API int spruce_tree_candidates(const int64_t *selected, int64_t R, int64_t nq, int64_t S, int64_t radix,
+                                      int64_t nchild, const int64_t *child_starts, int64_t *cand, uint8_t *valid,
+                                      void *stream);
+
+/*
+ * The level's beam (:105-108): per row, the k best of C candidates by score
+ * (invalid ones count as the fp32 minimum), descending, ties to the lower
+ * position; out int64 [rows, k] = the candidate id, or -1 where it is
+ * invalid.  C <= 256, 1 <= k <= C.
+ */
+SPRUCE_API int spruce_tree_topk(const float *scores, const uint8_t *valid, const int64_t *cand, int64_t rows,
+                                int64_t C, int64_t k, int64_t *out, void *stream);
+
+/*
  * Fused flat-gate selection: scores (as spruce_gate_scores), causal /
  * sink / local-window masking, top-W with W = K - (local_window + 1) -
  * sink_blocks (ties to the lowest block id) and packing to selected_blocks

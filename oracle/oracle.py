@@ -344,3 +344,79 @@ def maxsim(qp: torch.Tensor, kp: torch.Tensor, ids: torch.Tensor | None = None) 
     out = torch.empty((R, nq, ncols), dtype=torch.float32)
     lib().oracle_maxsim(_ptr(qc), _ptr(kc), None if idc is None else _ptr(idc), R, nq, nk, ncols, P, p, _ptr(out))
     return out
+
+
+def _round_to(x: np.ndarray, dtype: torch.dtype) -> np.ndarray:
+    """fp32 values after a round trip through dtype (round to nearest even)."""
+    if dtype == torch.float32:
+        return x.astype(np.float32)
+    return torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)).to(dtype).float().numpy()
+
+
+def tree_merge(child: torch.Tensor, radix: int = 2) -> torch.Tensor:
+    """One key-tree level up (selector/tree.py:80-112) in the features' dtype.
+
+    Parent prototype 0 = round(round(sum of the valid children's prototype 0 in
+    fp32) / round(count)); prototypes 1.. = the children's prototypes with the
+    largest distance round(sum_d round(round(x - mean)^2)) (fp32 sum in d
+    order), descending, ties to the lower candidate.
+    """
+    dt = child.dtype
+    c = child.detach().cpu().float().numpy()                     # [R, n, P, d]
+    R, n, P, d = c.shape
+    npar = (n + radix - 1) // radix
+    out = np.empty((R, npar, P, d), dtype=np.float32)
+    for r in range(R):
+        for pn in range(npar):
+            kids = c[r, pn * radix:min((pn + 1) * radix, n)]        # [nv, P, d]
+            nv = kids.shape[0]
+            s = np.zeros(d, dtype=np.float32)
+            for k in range(nv):
+                s = (s + kids[k, 0]).astype(np.float32)
+            mean = _round_to(_round_to(s, dt) / _round_to(np.float32(nv), dt), dt).astype(np.float32)
+            out[r, pn, 0] = mean
+            if P == 1:
+                continue
+            cands = kids.reshape(nv * P, d)
+            dist = np.full(radix * P, -np.inf, dtype=np.float32)
+            for ci in range(nv * P):
+                diff = _round_to((cands[ci] - mean).astype(np.float32), dt)
+                sq = _round_to((diff * diff).astype(np.float32), dt)
+                acc = np.float32(0.0)
+                for x in range(d):
+                    acc = np.float32(acc + sq[x])
+                dist[ci] = _round_to(np.array([acc], dtype=np.float32), dt)[0]
+            order = np.lexsort((np.arange(radix * P), -dist))[:P - 1]
+            out[r, pn, 1:] = cands[order]
+    return torch.from_numpy(out).to(dt)
+
+
+def traverse_to_leaf_ids(q_proj: torch.Tensor, level_proj: list, level_starts: list, beam: int,
+                         radix: int = 2) -> torch.Tensor:
+    """scripts/eval_tree_traversal.py:60-113 on projected features.
+
+    q_proj [R, qb, P, p]; level_proj[l] [R, nodes_l, P, p] and level_starts[l]
+    [nodes_l] leaf-first.  Candidates are the children of each row's current
+    selection; valid when the parent is, the child exists and starts at or
+    before the row's block; scores are MaxSim with invalid ones at the fp32
+    minimum; the best min(beam, C, children) are kept (ties to the lower
+    position), invalid ones as -1.  Returns int64 [R, qb, k].
+    """
+    R, qb = q_proj.shape[:2]
+    sel = torch.zeros((R, qb, 1), dtype=torch.int64)
+    for lvl in range(len(level_proj) - 2, -1, -1):
+        kp, starts = level_proj[lvl], level_starts[lvl].cpu()
+        nchild = kp.shape[1]
+        cand = (sel[..., None] * radix + torch.arange(radix)).flatten(-2)
+        valid = (sel[..., None] >= 0).expand(*sel.shape, radix).flatten(-2) & (cand < nchild)
+        safe = cand.clamp(0, nchild - 1)
+        valid &= starts[safe] <= torch.arange(qb)[None, :, None]
+        scores = maxsim(q_proj, kp, safe)
+        masked = torch.where(valid, scores, torch.full_like(scores, torch.finfo(torch.float32).min))
+        k = min(beam, cand.shape[-1], nchild)
+        C = cand.shape[-1]
+        pos = torch.arange(C).expand_as(masked)
+        order = torch.from_numpy(np.lexsort((pos.numpy().reshape(-1, C), -masked.numpy().reshape(-1, C))))
+        top = order.view(R, qb, C)[..., :k]
+        sel = torch.where(valid.gather(-1, top), safe.gather(-1, top), torch.full_like(top, -1))
+    return sel

@@ -39,6 +39,9 @@ SIGNATURES = {
     "spruce_pool_qk_protos": ([_P, _P, _P, _P, _INT, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _P], _INT),
     "spruce_gate_project": ([_P, _INT, _I64, _I64, _P, _I64, _P, _P], _INT),
     "spruce_gate_maxsim": ([_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P], _INT),
+    "spruce_tree_merge": ([_P, _INT, _I64, _I64, _I64, _I64, _I64, _P, _P], _INT),
+    "spruce_tree_candidates": ([_P, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P], _INT),
+    "spruce_tree_topk": ([_P, _P, _P, _I64, _I64, _I64, _P, _P], _INT),
     "spruce_gate_scores": ([_P, _P, _I64, _I64, _I64, _I64, _P, _P], _INT),
     "spruce_gate_select": ([_P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _P], _INT),
     "spruce_gate_select_rows": ([_P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _I64, _I64, _P], _INT),

@@ -192,6 +192,47 @@ int spruce_gate_maxsim(const float* qp, const float* kp, const int64_t* ids, int
                      "maxsim launch");
 }
 
+int spruce_tree_merge(const void* child, int dtype, int64_t R, int64_t nchild, int64_t P, int64_t d, int64_t radix,
+                      void* parent, void* stream) {
+  if (!valid_dtype(dtype)) return fail(SPRUCE_ERR_INVALID, "unsupported dtype code %d", dtype);
+  if (radix < 2) return fail(SPRUCE_ERR_INVALID, "radix must be >= 2, got %lld", (long long)radix);
+  if (R < 0 || nchild < 1 || d < 1 || d > 4096 || nchild > INT32_MAX) return fail(SPRUCE_ERR_INVALID, "bad tree shape");
+  if (P < 1 || P > 8 || radix * P > 256)
+    return fail(SPRUCE_ERR_UNSUPPORTED, "tree merge takes 1 to 8 prototypes and radix * P <= 256");
+  cudaError_t e;
+  switch (dtype) {
+    case SPRUCE_DTYPE_F32:
+      e = spruce::launch_tree_merge<float>(child, R, (int)nchild, parent, (int)P, (int)d, (int)radix, as_stream(stream));
+      break;
+    case SPRUCE_DTYPE_BF16:
+      e = spruce::launch_tree_merge<__nv_bfloat16>(child, R, (int)nchild, parent, (int)P, (int)d, (int)radix,
+                                                   as_stream(stream));
+      break;
+    default:
+      e = spruce::launch_tree_merge<__half>(child, R, (int)nchild, parent, (int)P, (int)d, (int)radix,
+                                            as_stream(stream));
+      break;
+  }
+  return cuda_status(e, "tree merge launch");
+}
+
+int spruce_tree_candidates(const int64_t* selected, int64_t R, int64_t nq, int64_t S, int64_t radix, int64_t nchild,
+                           const int64_t* child_starts, int64_t* cand, uint8_t* valid, void* stream) {
+  if (radix < 2 || R < 0 || nq < 0 || S < 1 || nchild < 1 || nq > INT32_MAX || nchild > INT32_MAX ||
+      S * radix > 256)
+    return fail(SPRUCE_ERR_INVALID, "bad traversal shape");
+  return cuda_status(spruce::launch_tree_candidates(selected, R, (int)nq, (int)S, (int)radix, (int)nchild,
+                                                    child_starts, cand, valid, as_stream(stream)),
+                     "tree candidate launch");
+}
+
+int spruce_tree_topk(const float* scores, const uint8_t* valid, const int64_t* cand, int64_t rows, int64_t C,
+                     int64_t k, int64_t* out, void* stream) {
+  if (rows < 0 || C < 1 || C > 256 || k < 1 || k > C) return fail(SPRUCE_ERR_INVALID, "bad traversal top-k shape");
+  return cuda_status(spruce::launch_tree_topk(scores, valid, cand, rows, (int)C, (int)k, out, as_stream(stream)),
+                     "tree top-k launch");
+}
+
 int spruce_gate_scores(const float* qp, const float* kp, int64_t R, int64_t qb, int64_t kb, int64_t P, float* out,
                        void* stream) {
   if (R < 0 || qb < 0 || kb < 0 || P < 1 || P > 1024) return fail(SPRUCE_ERR_INVALID, "bad score shape");

@@ -28,6 +28,15 @@ template <typename T>
 cudaError_t launch_project_rows(const void* x, int64_t groups, int qb, int row0, int nrows, int D, const float* W,
                                 int P, float* out, cudaStream_t stream);
 
+// Key tree of the deployed selector (tree.cu).
+template <typename T>
+cudaError_t launch_tree_merge(const void* child, int64_t R, int nchild, void* parent, int P, int d, int radix,
+                              cudaStream_t stream);
+cudaError_t launch_tree_candidates(const int64_t* sel, int64_t R, int nq, int S, int radix, int nchild,
+                                   const int64_t* child_starts, int64_t* cand, uint8_t* valid, cudaStream_t stream);
+cudaError_t launch_tree_topk(const float* scores, const uint8_t* valid, const int64_t* cand, int64_t rows, int C,
+                             int k, int64_t* out, cudaStream_t stream);
+
 // MaxSim scores (P prototypes of dimension pdim per row / key): every column
 // (ids == null, ncols == nk) or the candidate key ids[r, q, c].
 cudaError_t launch_maxsim(const float* qp, const float* kp, const int64_t* ids, int64_t R, int nq, int nk, int ncols,

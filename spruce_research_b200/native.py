@@ -335,3 +335,39 @@ def kv_summary_table(key: torch.Tensor, value: torch.Tensor, node_starts: torch.
         out["counts"].data_ptr(), out["log_counts"].data_ptr(), out["range_starts"].data_ptr(),
         out["range_ends"].data_ptr(), ws.data_ptr(), ws_bytes, _lib.stream_of(key)))
     return out
+
+
+def tree_merge(child: torch.Tensor, radix: int = 2) -> torch.Tensor:
+    """One key-tree level up (selector/tree.py:80-112): child [R, n, P, d] -> parent [R, ceil(n / radix), P, d]."""
+    _lib.require_cuda(child)
+    R, n, P, d = child.shape
+    child = child.contiguous()
+    out = torch.empty((R, (n + radix - 1) // radix, P, d), device=child.device, dtype=child.dtype)
+    _lib.check(_lib.load().spruce_tree_merge(child.data_ptr(), _dt(child), R, n, P, d, radix, out.data_ptr(),
+                                             _lib.stream_of(child)))
+    return out
+
+
+def tree_candidates(selected: torch.Tensor, radix: int, child_count: int, child_starts: torch.Tensor):
+    """Children of each row's selection: (cand int64 [R, nq, S*radix], valid bool) (eval_tree_traversal.py:83-95)."""
+    _lib.require_cuda(selected, child_starts)
+    R, nq, S = selected.shape
+    selected = selected.to(torch.int64).contiguous()
+    starts = child_starts.to(device=selected.device, dtype=torch.int64).contiguous()
+    cand = torch.empty((R, nq, S * radix), device=selected.device, dtype=torch.int64)
+    valid = torch.empty((R, nq, S * radix), device=selected.device, dtype=torch.uint8)
+    _lib.check(_lib.load().spruce_tree_candidates(selected.data_ptr(), R, nq, S, radix, child_count,
+                                                  starts.data_ptr(), cand.data_ptr(), valid.data_ptr(),
+                                                  _lib.stream_of(selected)))
+    return cand, valid
+
+
+def tree_topk(scores: torch.Tensor, valid: torch.Tensor, cand: torch.Tensor, k: int) -> torch.Tensor:
+    """The level's beam: int64 [R, nq, k] candidate ids, -1 where invalid (eval_tree_traversal.py:104-108)."""
+    _lib.require_cuda(scores, valid, cand)
+    R, nq, C = scores.shape
+    out = torch.empty((R, nq, k), device=scores.device, dtype=torch.int64)
+    _lib.check(_lib.load().spruce_tree_topk(scores.contiguous().data_ptr(), valid.contiguous().data_ptr(),
+                                            cand.contiguous().data_ptr(), R * nq, C, k, out.data_ptr(),
+                                            _lib.stream_of(scores)))
+    return out

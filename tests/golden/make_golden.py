@@ -209,6 +209,14 @@ def maxsim_cases(ref):
         cases[f"ms{n}_scores"] = s.numpy()
         cases[f"ms{n}_cand"] = cand.numpy()
         cases[f"ms{n}_cand_scores"] = sc.numpy()
+        # key tree (selector/tree.py:116) and beam traversal (scripts/eval_tree_traversal.py:60)
+        levels = ref["build_key_tree"](k_feat.float(), radix=2)
+        for lvl in levels:
+            cases[f"ms{n}_tree{lvl.level}"] = lvl.features.numpy()
+            cases[f"ms{n}_tree{lvl.level}_range"] = torch.stack([lvl.starts, lvl.ends]).numpy()
+        with torch.no_grad():
+            ids = ref["traverse"](gate, q_feat.float(), levels, 4, radix=2)
+        cases[f"ms{n}_leaf_ids"] = ids.numpy()
     return cases
 
 
@@ -230,6 +238,10 @@ def main():
            "attention": sparse_prefill_attention_forward, "summary": build_kv_summary_table,
            "tree_layout": build_residual_tree_layout, "summary_nodes": build_residual_summary_nodes,
            "summary_density": residual_attention_density}
+    from selector.tree import build_key_tree
+    from scripts.eval_tree_traversal import traverse_to_leaf_ids
+    ref["build_key_tree"] = build_key_tree
+    ref["traverse"] = traverse_to_leaf_ids
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     if args.only == "summaries":
         np.savez_compressed(os.path.join(HERE, "summaries.npz"), **summary_cases(ref))

@@ -142,3 +142,26 @@ def test_maxsim_scores_match_reference():
         want_c = torch.from_numpy(z[f"ms{n}_cand_scores"])[0]
         assert (got_c - want_c).abs().max().item() <= 2e-6 * want_c.abs().max().item()
         assert torch.equal(got_c, torch.gather(got, 2, cand))
+
+
+def test_key_tree_and_traversal_match_reference():
+    # selector/tree.py:116 build_key_tree and scripts/eval_tree_traversal.py:60
+    # traverse_to_leaf_ids (beam 4, radix 2) on the reference's fp32 features
+    z = load_npz("maxsim")
+    for n in range(2):
+        q, k, wq, wk = _maxsim_case(z, n)
+        qf = O.proto_pool_seq(q, 64, 8)[0].float()          # [G, nb, 8, d]
+        level = torch.from_numpy(z[f"ms{n}_tree0"])[0]      # the reference's leaf features (fp32)
+        assert torch.equal(level, O.proto_pool_seq(k, 64, 8)[0].float())
+        levels, starts = [level], [torch.from_numpy(z[f"ms{n}_tree0_range"])[0]]
+        l = 1
+        while f"ms{n}_tree{l}" in z:
+            level = O.tree_merge(level)
+            assert torch.equal(level, torch.from_numpy(z[f"ms{n}_tree{l}"])[0]), f"case {n} level {l}"
+            levels.append(level)
+            starts.append(torch.from_numpy(z[f"ms{n}_tree{l}_range"])[0])
+            l += 1
+        assert levels[-1].shape[1] == 1
+        proj = [O.project(x, wk[0]) for x in levels]
+        ids = O.traverse_to_leaf_ids(O.project(qf, wq[0]), proj, starts, beam=4)
+        assert torch.equal(ids, torch.from_numpy(z[f"ms{n}_leaf_ids"])[0])
