@@ -746,56 +746,82 @@ namespace spruce {
 // with key(c) = c (every key column) or ids[r, q, c] clamped to [0, nk) (the
 // candidate nodes of a tree level).  Every dot is one fma chain over p in
 // order, the max is exact in any order.  One CTA per (r, q): the row's P
-// query prototypes are staged in shared memory, each thread scores columns
-// c = tid, tid + 128, ... with P accumulators (one per key prototype) per
-// query prototype.
-template <int PMAX>
-__global__ void __launch_bounds__(128) maxsim_kernel(const float* __restrict__ qp, const float* __restrict__ kp,
-                                                     const int64_t* __restrict__ ids, int nq, int nk, int ncols,
-                                                     int P, int pdim, float denom, float* __restrict__ out) {
-  extern __shared__ float qsm[];  // [P][pdim]
-  const int64_t rq = blockIdx.x;  // r * nq + q
+// query prototypes and a batch of G = 128 / (P*P) candidates' key prototypes
+// are staged in shared memory (rows padded by one float against bank
+// conflicts); thread t computes the dot (i, j) = ((t % P^2) / P, t % P) of
+// candidate t / P^2, and the first G threads take the max over each
+// candidate's P^2 dots.
+constexpr int kMaxsimThreads = 128;
+
+__global__ void __launch_bounds__(kMaxsimThreads) maxsim_kernel(const float* __restrict__ qp,
+                                                               const float* __restrict__ kp,
+                                                               const int64_t* __restrict__ ids, int nq, int nk,
+                                                               int ncols, int P, int pdim, float denom,
+                                                               float* __restrict__ out) {
+  extern __shared__ float msm[];
+  const int stride = pdim + 1;
+  const int PP = P * P;
+  const int G = kMaxsimThreads / PP;
+  float* qs = msm;                      // [P][stride]
+  float* ks = qs + P * stride;          // [G][P][stride]
+  float* dots = ks + G * P * stride;    // [kMaxsimThreads]
+  const int64_t rq = blockIdx.x;        // r * nq + q
   const int64_t r = rq / nq;
-  for (int e = threadIdx.x; e < P * pdim; e += 128) qsm[e] = qp[rq * P * pdim + e];
-  __syncthreads();
-  for (int c = threadIdx.x; c < ncols; c += 128) {
-    int64_t key = c;
-    if (ids != nullptr) {
-      key = ids[rq * ncols + c];
-      key = key < 0 ? 0 : (key >= nk ? nk - 1 : key);
-    }
-    const float* kr = kp + (r * nk + key) * P * pdim;
-    float best = -INFINITY;
-    for (int i = 0; i < P; ++i) {
-      const float* qi = qsm + i * pdim;
-      float acc[PMAX];
-#pragma unroll
-      for (int j = 0; j < PMAX; ++j) acc[j] = 0.0f;
-      for (int x = 0; x < pdim; ++x) {
-        const float qv = qi[x];
-#pragma unroll
-        for (int j = 0; j < PMAX; ++j)
-          if (j < P) acc[j] = __fmaf_rn(qv, __ldg(kr + j * pdim + x), acc[j]);
+  for (int e = threadIdx.x; e < P * pdim; e += kMaxsimThreads) qs[(e / pdim) * stride + e % pdim] = qp[rq * P * pdim + e];
+  const int slot = threadIdx.x / PP, i = (threadIdx.x % PP) / P, j = threadIdx.x % P;
+  for (int c0 = 0; c0 < ncols; c0 += G) {
+    __syncthreads();  // qs ready / previous batch's ks and dots consumed
+    const int nb = min(G, ncols - c0);
+    for (int e = threadIdx.x; e < nb * P * pdim; e += kMaxsimThreads) {
+      const int g = e / (P * pdim), rest = e % (P * pdim);
+      int64_t key = c0 + g;
+      if (ids != nullptr) {
+        key = ids[rq * ncols + c0 + g];
+        key = key < 0 ? 0 : (key >= nk ? nk - 1 : key);
       }
-#pragma unroll
-      for (int j = 0; j < PMAX; ++j)
-        if (j < P) best = fmaxf(best, acc[j]);
+      ks[(g * P + rest / pdim) * stride + rest % pdim] = __ldg(kp + (r * nk + key) * P * pdim + rest);
     }
-    out[rq * ncols + c] = __fdiv_rn(best, denom);
+    __syncthreads();
+    float acc = -INFINITY;
+    if (slot < nb) {
+      const float* qi = qs + i * stride;
+      const float* kj = ks + (slot * P + j) * stride;
+      acc = 0.0f;
+      for (int x = 0; x < pdim; ++x) acc = __fmaf_rn(qi[x], kj[x], acc);
+    }
+    if (PP == 64) {  // P = 8: a candidate's dots fill two whole warps
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) acc = fmaxf(acc, __shfl_xor_sync(0xffffffffu, acc, off));
+      if ((threadIdx.x & 31) == 0) dots[threadIdx.x >> 5] = acc;
+      __syncthreads();
+      if (threadIdx.x < nb)
+        out[rq * ncols + c0 + threadIdx.x] = __fdiv_rn(fmaxf(dots[2 * threadIdx.x], dots[2 * threadIdx.x + 1]), denom);
+    } else {
+      dots[threadIdx.x] = acc;
+      __syncthreads();
+      if (threadIdx.x < nb) {
+        float best = -INFINITY;
+        for (int e = 0; e < PP; ++e) best = fmaxf(best, dots[threadIdx.x * PP + e]);
+        out[rq * ncols + c0 + threadIdx.x] = __fdiv_rn(best, denom);
+      }
+    }
   }
 }
 
 cudaError_t launch_maxsim(const float* qp, const float* kp, const int64_t* ids, int64_t R, int nq, int nk, int ncols,
                           int P, int pdim, float* out, cudaStream_t stream) {
   if (R * nq == 0 || ncols == 0) return cudaSuccess;
+  if (P < 1 || P > 8) return cudaErrorInvalidValue;
   const float denom = static_cast<float>(std::sqrt(static_cast<double>(pdim)));
-  const size_t smem = sizeof(float) * (size_t)P * pdim;
+  const int G = kMaxsimThreads / (P * P);
+  const size_t smem = sizeof(float) * ((size_t)(1 + G) * P * (pdim + 1) + kMaxsimThreads);
+  if (smem > 227 * 1024) return cudaErrorInvalidValue;
   if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(maxsim_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(maxsim_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
-  if (P > 8) return cudaErrorInvalidValue;
-  maxsim_kernel<8><<<(unsigned)(R * nq), 128, smem, stream>>>(qp, kp, ids, nq, nk, ncols, P, pdim, denom, out);
+  maxsim_kernel<<<(unsigned)(R * nq), kMaxsimThreads, smem, stream>>>(qp, kp, ids, nq, nk, ncols, P, pdim, denom,
+                                                                      out);
   return cudaGetLastError();
 }
 
