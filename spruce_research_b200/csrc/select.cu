@@ -808,11 +808,225 @@ __global__ void __launch_bounds__(kMaxsimThreads) maxsim_kernel(const float* __r
   }
 }
 
+// MaxSim with one candidate per lane: a one-warp CTA per (r, q) row scores
+// 32 candidates at a time, each lane holding all P*P dot products of its
+// candidate in registers.  Query prototypes are read as broadcasts, the
+// candidates' prototypes are staged by cp.async in chunks of kMsChunk
+// elements of p into two alternating buffers (candidate rows padded to
+// P*kMsChunk + 4 floats, so a quarter-warp's float4 reads hit distinct
+// banks).  Each dot is the same in-order fma chain over p as maxsim_kernel.
+constexpr int kMsChunk = 16;
+
+template <int P>
+__global__ void __launch_bounds__(32) maxsim_lane_kernel(const float* __restrict__ qp, const float* __restrict__ kp,
+                                                         const int64_t* __restrict__ ids, int nq, int nk, int ncols,
+                                                         int pdim, float denom, float* __restrict__ out) {
+  constexpr int KS = P * kMsChunk + 4;     // floats per staged candidate
+  constexpr int QV = P * kMsChunk / 4;     // float4 copies of one query chunk
+  constexpr int KV = 32 * P * kMsChunk / 4;  // float4 copies of one candidate chunk
+  constexpr int STAGE = 32 * KS + P * kMsChunk;
+  extern __shared__ __align__(16) float lsm[];
+  const int lane = threadIdx.x;
+  const int64_t rq = blockIdx.x;
+  const int64_t r = rq / nq;
+  const float* qrow = qp + rq * P * pdim;
+  const int nch = pdim / kMsChunk;
+  for (int c0 = 0; c0 < ncols; c0 += 32) {
+    const int nb = min(32, ncols - c0);
+    int64_t mykey = c0 + lane;
+    if (ids != nullptr && lane < nb) mykey = ids[rq * ncols + c0 + lane];
+    mykey = mykey < 0 ? 0 : (mykey >= nk ? nk - 1 : mykey);
+    const float* krow = kp + (r * nk + mykey) * P * pdim;
+    auto stage = [&](int ch) {
+      float* buf = lsm + (ch & 1) * STAGE;
+      float* qs = buf + 32 * KS;
+      const int x0 = ch * kMsChunk;
+      for (int e = lane; e < QV; e += 32) {
+        const int i = e / (kMsChunk / 4), v = e % (kMsChunk / 4);
+        cp_async16(qs + i * kMsChunk + 4 * v, qrow + (int64_t)i * pdim + x0 + 4 * v, 16);
+      }
+#pragma unroll 4
+      for (int e = lane; e < KV; e += 32) {
+        const int c = e / (P * kMsChunk / 4), rest = e % (P * kMsChunk / 4);
+        const int j = rest / (kMsChunk / 4), v = rest % (kMsChunk / 4);
+        const float* src = reinterpret_cast<const float*>(
+            __shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(krow), c));
+        if (c < nb) cp_async16(buf + c * KS + j * kMsChunk + 4 * v, src + (int64_t)j * pdim + x0 + 4 * v, 16);
+      }
+      cp_async_commit();
+    };
+    float acc[P][P];
+#pragma unroll
+    for (int i = 0; i < P; ++i)
+#pragma unroll
+      for (int j = 0; j < P; ++j) acc[i][j] = 0.0f;
+    stage(0);
+    for (int ch = 0; ch < nch; ++ch) {
+      if (ch + 1 < nch) {
+        stage(ch + 1);
+        cp_async_wait<1>();
+      } else {
+        cp_async_wait<0>();
+      }
+      __syncwarp();
+      const float* buf = lsm + (ch & 1) * STAGE;
+      const float* qs = buf + 32 * KS;
+      const float* ks = buf + lane * KS;
+#pragma unroll
+      for (int v = 0; v < kMsChunk / 4; ++v) {
+        float4 qv[P];
+#pragma unroll
+        for (int i = 0; i < P; ++i) qv[i] = *reinterpret_cast<const float4*>(qs + i * kMsChunk + 4 * v);
+#pragma unroll
+        for (int j = 0; j < P; ++j) {
+          const float4 kv = *reinterpret_cast<const float4*>(ks + j * kMsChunk + 4 * v);
+#pragma unroll
+          for (int i = 0; i < P; ++i) {
+            float a = acc[i][j];
+            a = __fmaf_rn(qv[i].x, kv.x, a);
+            a = __fmaf_rn(qv[i].y, kv.y, a);
+            a = __fmaf_rn(qv[i].z, kv.z, a);
+            acc[i][j] = __fmaf_rn(qv[i].w, kv.w, a);
+          }
+        }
+      }
+      __syncwarp();  // this buffer is restaged two chunks on
+    }
+    float best = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < P; ++i)
+#pragma unroll
+      for (int j = 0; j < P; ++j) best = fmaxf(best, acc[i][j]);
+    if (lane < nb) out[rq * ncols + c0 + lane] = __fdiv_rn(best, denom);
+  }
+}
+
+// MaxSim for a level of at most 32 nodes (the top of the key tree), where
+// every query row's candidates come from the same few nodes: a persistent
+// CTA stages all nk nodes' prototypes of one r in shared memory once (node
+// rows padded to P*p + 4 floats for conflict-free float4 reads) and its warps
+// score whole rows, lane = (row slot, node), nkpad = next power of two >= nk
+// nodes per row slot.  A row's candidate scores are then shuffled out of the
+// lanes that hold the candidates' nodes.  Same in-order fma chain per dot.
+template <int P>
+__global__ void __launch_bounds__(256) maxsim_nodes_kernel(const float* __restrict__ qp, const float* __restrict__ kp,
+                                                           const int64_t* __restrict__ ids, int nq, int nk, int nkpad,
+                                                           int ncols, int pdim, float denom, float* __restrict__ out) {
+  extern __shared__ __align__(16) float nsm[];
+  const int NS = P * pdim + 4;
+  const int64_t r = blockIdx.y;
+  const float* kr = kp + r * nk * P * pdim;
+  for (int e = threadIdx.x; e < nk * P * pdim / 4; e += blockDim.x) {
+    const int n = e / (P * pdim / 4), rest = e % (P * pdim / 4);
+    cp_async16(nsm + n * NS + 4 * rest, kr + 4 * (int64_t)e, 16);
+  }
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int rpw = 32 / nkpad, sub = lane / nkpad, n = lane % nkpad;
+  const int groups = (nq + rpw - 1) / rpw;
+  const float* ks = nsm + min(n, nk - 1) * NS;  // only nk node rows are staged; lanes n >= nk are never read out
+  for (int g = blockIdx.x * nwarps + warp; g < groups; g += gridDim.x * nwarps) {  // uniform per warp
+    const int q = g * rpw + sub;
+    const bool live = q < nq;
+    const int64_t rq = r * nq + (live ? q : nq - 1);
+    const float* qrow = qp + rq * P * pdim;
+    float acc[P][P];
+#pragma unroll
+    for (int i = 0; i < P; ++i)
+#pragma unroll
+      for (int j = 0; j < P; ++j) acc[i][j] = 0.0f;
+#pragma unroll 2
+    for (int v = 0; v < pdim / 4; ++v) {
+      float4 qv[P];
+#pragma unroll
+      for (int i = 0; i < P; ++i) qv[i] = __ldg(reinterpret_cast<const float4*>(qrow + i * pdim) + v);
+#pragma unroll
+      for (int j = 0; j < P; ++j) {
+        const float4 kv = *reinterpret_cast<const float4*>(ks + j * pdim + 4 * v);
+#pragma unroll
+        for (int i = 0; i < P; ++i) {
+          float a = acc[i][j];
+          a = __fmaf_rn(qv[i].x, kv.x, a);
+          a = __fmaf_rn(qv[i].y, kv.y, a);
+          a = __fmaf_rn(qv[i].z, kv.z, a);
+          acc[i][j] = __fmaf_rn(qv[i].w, kv.w, a);
+        }
+      }
+    }
+    float best = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < P; ++i)
+#pragma unroll
+      for (int j = 0; j < P; ++j) best = fmaxf(best, acc[i][j]);
+    const float score = __fdiv_rn(best, denom);
+    if (ids == nullptr) {
+      if (live && n < nk) out[rq * ncols + n] = score;
+      continue;
+    }
+    for (int cb = 0; cb < ncols; cb += nkpad) {  // same trip count in every lane
+      const int c = cb + n;
+      const bool w = live && c < ncols;
+      int64_t key = w ? ids[rq * ncols + c] : 0;
+      key = key < 0 ? 0 : (key >= nk ? nk - 1 : key);
+      const float s = __shfl_sync(0xffffffffu, score, sub * nkpad + (int)key);
+      if (w) out[rq * ncols + c] = s;
+    }
+  }
+}
+
+template <int P>
+cudaError_t launch_maxsim_nodes(const float* qp, const float* kp, const int64_t* ids, int64_t R, int nq, int nk,
+                                int ncols, int pdim, float denom, float* out, cudaStream_t stream) {
+  int nkpad = 1;
+  while (nkpad < nk) nkpad <<= 1;
+  const size_t smem = sizeof(float) * (size_t)nk * (P * pdim + 4);
+  cudaError_t e = cudaFuncSetAttribute(maxsim_nodes_kernel<P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return e;
+  const int rows_per_warp = 32 / nkpad;
+  const int64_t groups = (nq + rows_per_warp - 1) / rows_per_warp;
+  const int64_t per_r = std::max<int64_t>(1, std::min<int64_t>((148 + R - 1) / R, (groups + 7) / 8));
+  maxsim_nodes_kernel<P><<<dim3((unsigned)per_r, (unsigned)R), 256, smem, stream>>>(qp, kp, ids, nq, nk, nkpad,
+                                                                                    ncols, pdim, denom, out);
+  return cudaGetLastError();
+}
+
+template <int P>
+cudaError_t launch_maxsim_lane(const float* qp, const float* kp, const int64_t* ids, int64_t R, int nq, int nk,
+                               int ncols, int pdim, float denom, float* out, cudaStream_t stream) {
+  const size_t smem = sizeof(float) * 2 * (32 * (P * kMsChunk + 4) + P * kMsChunk);
+  maxsim_lane_kernel<P><<<(unsigned)(R * nq), 32, smem, stream>>>(qp, kp, ids, nq, nk, ncols, pdim, denom, out);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_maxsim(const float* qp, const float* kp, const int64_t* ids, int64_t R, int nq, int nk, int ncols,
                           int P, int pdim, float* out, cudaStream_t stream) {
   if (R * nq == 0 || ncols == 0) return cudaSuccess;
   if (P < 1 || P > 8) return cudaErrorInvalidValue;
   const float denom = static_cast<float>(std::sqrt(static_cast<double>(pdim)));
+  const bool lane_ok = pdim % kMsChunk == 0 && pdim > 0 &&
+                       ((reinterpret_cast<uintptr_t>(qp) | reinterpret_cast<uintptr_t>(kp)) & 15) == 0;
+  const size_t nodes_smem = sizeof(float) * (size_t)nk * (P * pdim + 4);
+  if (lane_ok && P >= 4 && nk <= 32 && nodes_smem <= 227 * 1024 && R <= 65535) {
+    switch (P) {
+      case 4: return launch_maxsim_nodes<4>(qp, kp, ids, R, nq, nk, ncols, pdim, denom, out, stream);
+      case 5: return launch_maxsim_nodes<5>(qp, kp, ids, R, nq, nk, ncols, pdim, denom, out, stream);
+      case 6: return launch_maxsim_nodes<6>(qp, kp, ids, R, nq, nk, ncols, pdim, denom, out, stream);
+      case 7: return launch_maxsim_nodes<7>(qp, kp, ids, R, nq, nk, ncols, pdim, denom, out, stream);
+      default: return launch_maxsim_nodes<8>(qp, kp, ids, R, nq, nk, ncols, pdim, denom, out, stream);
+    }
+  }
+  if (lane_ok && P >= 4) {
+    switch (P) {
+      case 4: return launch_maxsim_lane<4>(qp, kp, ids, R, nq, nk, ncols, pdim, denom, out, stream);
+      case 5: return launch_maxsim_lane<5>(qp, kp, ids, R, nq, nk, ncols, pdim, denom, out, stream);
+      case 6: return launch_maxsim_lane<6>(qp, kp, ids, R, nq, nk, ncols, pdim, denom, out, stream);
+      case 7: return launch_maxsim_lane<7>(qp, kp, ids, R, nq, nk, ncols, pdim, denom, out, stream);
+      default: return launch_maxsim_lane<8>(qp, kp, ids, R, nq, nk, ncols, pdim, denom, out, stream);
+    }
+  }
   const int G = kMaxsimThreads / (P * P);
   const size_t smem = sizeof(float) * ((size_t)(1 + G) * P * (pdim + 1) + kMaxsimThreads);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;

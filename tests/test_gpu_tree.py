@@ -10,6 +10,7 @@ import torch
 
 from golden_cases import load_npz
 from oracle import oracle as O
+from spruce_research_b200 import native
 from spruce_research_b200.selector.gate import FlatGate
 from spruce_research_b200.selector.tree import build_key_tree, traverse_to_leaf_ids, tree_select_blocks
 from spruce_research_b200.synthetic import LayerShape, make_layer_inputs
@@ -77,3 +78,23 @@ def test_deployed_selector_matches_oracle_composition():
     want = O.selected_ids_to_blocks(ids[None], beam + lw + 1, lw, qb, 0)[0, 0]
     assert torch.equal(sel[0].cpu(), want)
     O.validate_selected_blocks(sel[:, None].cpu().contiguous(), local_window=lw)
+
+
+@pytest.mark.parametrize("nk", [70, 32, 17, 5, 1])
+@pytest.mark.parametrize("P,p", [(8, 64), (5, 48), (4, 16), (3, 64), (8, 40), (1, 32)])
+def test_maxsim_shapes_match_oracle(P, p, nk):
+    # node-staged kernel (nk <= 32), lane-per-candidate kernel (P >= 4,
+    # p % 16 == 0, 16-byte aligned) and the general kernel, over more than one
+    # 32-candidate group and clamped ids
+    gen = torch.Generator().manual_seed(64 + P * p + nk)
+    R, nq, C = 3, 41, 37
+    qp = torch.randn((R, nq, P, p), generator=gen)
+    kp = torch.randn((R, nk, P, p), generator=gen)
+    ids = torch.randint(-2, nk + 2, (R, nq, C), generator=gen)
+    assert torch.equal(native.gate_maxsim(qp.cuda(), kp.cuda()).cpu(), O.maxsim(qp, kp))
+    assert torch.equal(native.gate_maxsim(qp.cuda(), kp.cuda(), ids.cuda()).cpu(), O.maxsim(qp, kp, ids))
+    # a view 4 bytes past an aligned allocation takes the general kernel
+    flat = torch.empty(qp.numel() + 1, device="cuda")
+    shifted = flat[1:].view(qp.shape)
+    shifted.copy_(qp.cuda())
+    assert torch.equal(native.gate_maxsim(shifted, kp.cuda(), ids.cuda()).cpu(), O.maxsim(qp, kp, ids))
