@@ -10,6 +10,7 @@ are all-gathered over NCCL; total work is fixed, so scaling is strong.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
     python bench.py --sweep          # config 4: variable-length batch, densities 2..100%
+    python bench.py --model          # config 3: whole-model prefill TTFT, dense vs SPRUCE flows
 
 `value` is effective TFLOP/s of the selected tiles (algorithmic FLOPs of the
 step / device time of the step, max over ranks); `e2e` is the same metric
@@ -83,6 +84,9 @@ def parse_args():
                     help="N>1 output all-gather: NVLink peer stores in the attention epilogue, or NCCL")
     ap.add_argument("--sweep", action="store_true",
                     help="config 4 instead: 8 variable-length sequences, densities 2..100%%, one GPU")
+    ap.add_argument("--model", action="store_true",
+                    help="config 3 instead: whole Qwen2-7B-shaped model prefill TTFT, dense vs SPRUCE flows")
+    ap.add_argument("--model-tokens", type=int, default=65536)
     return ap.parse_args()
 
 
@@ -559,6 +563,129 @@ def run_sweep(args):
     emit(result)
 
 
+def run_model(args):
+    """prefill of a random-init bf16 Qwen2-7B-shaped model (hidden 3584, FFN 18944,
+    28 layers, 28/4 heads, vocab 152064, RoPE base 1e6 with YaRN factor 4) on seeded random token ids.
+
+    Each flow's TTFT is timed with CUDA events from the pinned host token ids to the first generated
+    token id back in pinned host memory: the dense SDPA model, and SPRUCE's one-pass (route inside each
+    layer's attention call) and two-pass (dense feature capture, routing, sparse forward) flows with the
+    flat gate at ``--density`` and the deployed tree gate (P=8, beam 16).  The random-init model's last
+    logits at 10% density need not resemble the dense model's; the all-blocks flow (every causal block
+    selected) must."""
+    import math
+
+    import torch
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+
+    from spruce_research_b200.kernels.sparse_prefill import SPRUCE_TRITON_SPARSE_PREFILL
+    from spruce_research_b200.live import LiveSelector, capture_selector_features, sparse_prefill
+    from spruce_research_b200.selector.gate import FlatGate
+    from spruce_research_b200.synthetic import causal_block_entries
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    T = args.model_tokens
+    cfg = Qwen2Config(vocab_size=152064, hidden_size=3584, intermediate_size=18944, num_hidden_layers=28,
+                      num_attention_heads=28, num_key_value_heads=4, max_position_embeddings=131072,
+                      rope_parameters={"rope_type": "yarn", "factor": 4.0, "original_max_position_embeddings": 32768,
+                                       "rope_theta": 1e6})
+    torch.manual_seed(args.seed)
+    default = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        with torch.device(dev):
+            model = Qwen2ForCausalLM(cfg).eval()
+            gate = FlatGate(28, 128, 128).float().eval()
+    finally:
+        torch.set_default_dtype(default)
+    model.set_attn_implementation("sdpa")
+    ids_host = torch.randint(0, cfg.vocab_size, (1, T), generator=torch.Generator().manual_seed(args.seed + 3))
+    ids_host = ids_host.pin_memory()
+    tok_host = torch.empty((), dtype=torch.int64).pin_memory()
+    qb = math.ceil(T / 64)
+    flat = LiveSelector(gate, mode="flat", density=args.density, local_window=0, sink_blocks=1)
+    tree = LiveSelector(gate, mode="tree", beam=16, radix=2, prototypes=8, local_window=1, sink_blocks=0)
+    # every causal block: the sparse path must then reproduce the dense model
+    full = LiveSelector(gate, mode="flat", k_selected=qb, local_window=0, sink_blocks=1)
+
+    def two_pass(selector, marks):
+        def run(ids):
+            marks.append(torch.cuda.Event(enable_timing=True))
+            marks[-1].record()
+            feats = capture_selector_features(model, ids, selector.feature_prototypes)
+            marks.append(torch.cuda.Event(enable_timing=True))
+            marks[-1].record()
+            selected = selector.route(feats)
+            del feats
+            marks.append(torch.cuda.Event(enable_timing=True))
+            marks[-1].record()
+            model.set_attn_implementation(SPRUCE_TRITON_SPARSE_PREFILL)
+            try:
+                return model(ids, use_cache=True, logits_to_keep=1, selected_blocks=selected, block_size=64)
+            finally:
+                model.set_attn_implementation("sdpa")
+        return run
+
+    phase_marks = {"spruce_two_pass_flat": [], "spruce_two_pass_tree": []}
+    flows = {
+        "dense_sdpa": lambda ids: model(ids, use_cache=True, logits_to_keep=1),
+        "spruce_one_pass_flat": lambda ids: sparse_prefill(model, ids, flat, flow="one_pass")[0],
+        "spruce_two_pass_flat": two_pass(flat, phase_marks["spruce_two_pass_flat"]),
+        "spruce_one_pass_tree": lambda ids: sparse_prefill(model, ids, tree, flow="one_pass")[0],
+        "spruce_two_pass_tree": two_pass(tree, phase_marks["spruce_two_pass_tree"]),
+        "spruce_one_pass_all_blocks": lambda ids: sparse_prefill(model, ids, full, flow="one_pass")[0],
+    }
+    results, dense_logits = {}, None
+    with torch.no_grad():
+        for name, fn in flows.items():
+            times, logits = [], None
+            for it in range(max(1, args.warmup) + args.steps):
+                marks = phase_marks.get(name)
+                if marks is not None:
+                    marks.clear()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                torch.cuda.synchronize()
+                e0.record()
+                ids = ids_host.to(dev, non_blocking=True)
+                out = fn(ids)
+                tok_host.copy_(out.logits[0, -1].argmax(), non_blocking=True)
+                e1.record()
+                e1.synchronize()
+                if it >= max(1, args.warmup):
+                    times.append(e0.elapsed_time(e1))
+                logits = out.logits[0, -1].float()
+                del out
+            row = {"ttft_ms": statistics.median(times), "ttft_ms_all": times, "first_token": int(tok_host)}
+            if name in phase_marks:
+                m = phase_marks[name]
+                row["phases_ms_last_step"] = {"capture": m[0].elapsed_time(m[1]), "route": m[1].elapsed_time(m[2]),
+                                              "sparse_forward_and_first_token": m[2].elapsed_time(e1)}
+            if dense_logits is None:
+                dense_logits = logits
+            else:
+                row["last_logits_vs_dense"] = {
+                    "cosine": torch.nn.functional.cosine_similarity(logits, dense_logits, dim=0).item(),
+                    "max_abs": (logits - dense_logits).abs().max().item(),
+                    "same_first_token": row["first_token"] == results["dense_sdpa"]["first_token"]}
+            results[name] = row
+            torch.cuda.empty_cache()
+    K_flat = flat.width(qb)
+    flat_density = causal_block_entries(qb, K_flat) / (qb * (qb + 1) // 2)
+    one = results["spruce_one_pass_flat"]["ttft_ms"]
+    emit({
+        "metric": "config 3 prefill TTFT, Qwen2-7B-shaped random-init bf16 model",
+        "value": one, "unit": "ms", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": one, "higher_is_better": False, "dtype": "bf16",
+        "data": "synthetic: random-init weights (seeded), random token ids",
+        "config": {"workload": f"config 3: Qwen2-7B shape, {T} tokens, YaRN factor 4",
+                   "tokens": T, "query_blocks": qb, "flat_k_selected": K_flat, "flat_charged_density": flat_density,
+                   "tree": {"beam": 16, "prototypes": 8, "k_selected": tree.width(qb)}},
+        "flows": results,
+        "speedup_vs_dense": {k: results["dense_sdpa"]["ttft_ms"] / v["ttft_ms"] for k, v in results.items()},
+    })
+
+
 def main():
     args = parse_args()
     _claim_stdout()
@@ -566,6 +693,8 @@ def main():
         run_reference(args)
     elif args.sweep:
         run_sweep(args)
+    elif args.model:
+        run_model(args)
     else:
         run_b200(args)
 

@@ -80,6 +80,26 @@ def traverse_to_leaf_ids(gate, q_feat: torch.Tensor, key_levels: list[KeyTreeLev
 
 
 @torch.no_grad()
+def route_from_features(gate, q_feat: torch.Tensor, k_feat: torch.Tensor, beam: int = 16, radix: int = 2,
+                        local_window: int = 1, sink_blocks: int = 0, k_selected: int | None = None) -> torch.Tensor:
+    """Tree routes of captured features: int32 ``[L, G, qb, K]``.
+
+    ``q_feat`` / ``k_feat`` are ``[L, G, blocks, P, d]`` prototypes (one row
+    of layers per gate layer); the key tree, its beam traversal and
+    ``selected_ids_to_blocks`` follow benchmarks/compare_dense_sparse_live_tree.py:131-197
+    (K = beam + local_window + 1 unless given).
+    """
+    L, G, qb = q_feat.shape[:3]
+    if k_selected is None:
+        k_selected = beam + local_window + 1
+    levels = build_key_tree(k_feat, radix)
+    ids = traverse_to_leaf_ids(gate, q_feat, levels, beam, radix)          # [L, G, qb, C]
+    packed = native.pack_selected_ids(ids.reshape(L * G, qb, -1), k_selected, local_window, k_feat.shape[2],
+                                      sink_blocks)
+    return packed.view(L, G, qb, k_selected)
+
+
+@torch.no_grad()
 def tree_select_blocks(query: torch.Tensor, key: torch.Tensor, gate, beam: int = 16, radix: int = 2,
                        prototypes: int = 8, local_window: int = 1, sink_blocks: int = 0,
                        k_selected: int | None = None) -> torch.Tensor:
@@ -100,7 +120,6 @@ def tree_select_blocks(query: torch.Tensor, key: torch.Tensor, gate, beam: int =
     q_feat, k_feat = pool_selector_features(query, key, prototypes)       # [B, Hkv, qb, P, d]
     out = torch.empty((B, Hkv, qb, k_selected), device=query.device, dtype=torch.int32)
     for b in range(B):
-        levels = build_key_tree(k_feat[b][None], radix)
-        ids = traverse_to_leaf_ids(gate, q_feat[b][None], levels, beam, radix)    # [1, Hkv, qb, C]
-        out[b] = native.pack_selected_ids(ids[0], k_selected, local_window, qb, sink_blocks)
+        out[b] = route_from_features(gate, q_feat[b][None], k_feat[b][None], beam, radix, local_window,
+                                     sink_blocks, k_selected)[0]
     return out
