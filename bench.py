@@ -11,6 +11,7 @@ are all-gathered over NCCL; total work is fixed, so scaling is strong.
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
     python bench.py --sweep          # config 4: variable-length batch, densities 2..100%
     python bench.py --model          # config 3: whole-model prefill TTFT, dense vs SPRUCE flows
+    python bench.py --tree-selector  # deployed selector (P=8 prototypes, key tree, beam 16) ms/layer
 
 `value` is effective TFLOP/s of the selected tiles (algorithmic FLOPs of the
 step / device time of the step, max over ranks); `e2e` is the same metric
@@ -87,6 +88,8 @@ def parse_args():
     ap.add_argument("--model", action="store_true",
                     help="config 3 instead: whole Qwen2-7B-shaped model prefill TTFT, dense vs SPRUCE flows")
     ap.add_argument("--model-tokens", type=int, default=65536)
+    ap.add_argument("--tree-selector", action="store_true",
+                    help="time the deployed tree selector (P=8, beam 16) beside the flat one at config 2's shape")
     return ap.parse_args()
 
 
@@ -686,6 +689,57 @@ def run_model(args):
     })
 
 
+def run_tree_selector(args):
+    """The deployed selector at config 2's layer shape: P=8 outlier
+    prototypes, the key tree and a beam-16 traversal (K = 18), beside the flat P=1 selector (K at
+    ``--density``).  Device time per layer with CUDA events; selection only, no attention."""
+    import torch
+
+    from spruce_research_b200.pipeline import SparsePrefillLayer
+    from spruce_research_b200.selector.gate import FlatGate
+    from spruce_research_b200.selector.tree import tree_select_blocks
+    from spruce_research_b200.synthetic import LayerShape, k_for_density, make_gate_weights, make_layer_inputs
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    shape = LayerShape(1, 28, 4, args.tokens, 128)
+    q, k, _ = make_layer_inputs(shape, torch.bfloat16, args.seed, device=dev)
+    wq, wk = make_gate_weights(1, 128, 128, args.seed + 1, device=dev)
+    gate = FlatGate(1, 128, 128).to(dev).eval()
+    with torch.no_grad():
+        gate.Wq.copy_(wq)
+        gate.Wk.copy_(wk)
+    qb = (args.tokens + 63) // 64
+    flat = SparsePrefillLayer(wq[0], wk[0], k_for_density(qb, args.density), 0, 1)
+
+    def timed(fn):
+        for _ in range(max(1, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / args.steps
+
+    tree_ms = timed(lambda: tree_select_blocks(q, k, gate, beam=16, radix=2, prototypes=8))
+    flat_ms = timed(lambda: flat.select(q, k))
+    sel = tree_select_blocks(q, k, gate, beam=16, radix=2, prototypes=8)
+    emit({
+        "metric": "deployed tree selector ms/layer (P=8, beam 16) beside the flat selector",
+        "value": tree_ms, "unit": "ms", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": tree_ms, "higher_is_better": False, "dtype": "bf16 features, fp32 scores",
+        "data": "synthetic: seeded N(0,1) Q/K, RoPE base 1e6, planted affinity; kaiming-uniform gate",
+        "config": {"workload": f"config 2 layer shape, {args.tokens} tokens, 28Q/4KV, d=p=128",
+                   "tree": {"prototypes": 8, "beam": 16, "radix": 2, "k_selected": int(sel.shape[-1]),
+                            "entries_per_group": int((sel[0, 0] >= 0).sum())},
+                   "flat": {"k_selected": flat.k_selected}},
+        "flat_selector_ms": flat_ms,
+    })
+
+
 def main():
     args = parse_args()
     _claim_stdout()
@@ -695,6 +749,8 @@ def main():
         run_sweep(args)
     elif args.model:
         run_model(args)
+    elif args.tree_selector:
+        run_tree_selector(args)
     else:
         run_b200(args)
 
