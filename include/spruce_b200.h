@@ -329,6 +329,32 @@ SPRUCE_API int spruce_ipc_export(const void *ptr, void *handle, int64_t *offset)
 SPRUCE_API int spruce_ipc_import(const void *handle, int64_t offset, void **ptr, void **base);
 SPRUCE_API int spruce_ipc_close(void *base);
 
+/* Residual-summary attention (sparse/attention.py:83-274 with residual_summaries=True,
+ * replacing its per-(query block, KV group) loop at :178-263): the block-sparse attention of
+ * spruce_sparse_attention_fwd, where each row's softmax also covers the summary keys of its
+ * residual tree nodes.  nodes: int32 [B, Hkv, qb, S] residual node ids, -1 padded (one layer of
+ * residual_summary_nodes, interfaces/residual_summaries.py:158-220), element strides node_strides.
+ * The summary table is the output of spruce_kv_summary_table for the same K/V: keys and values
+ * fp32 [B, Hkv, num_nodes, prototypes, D], counts and log_counts fp32 [B, num_nodes, prototypes].
+ * A prototype with count > 0 adds the score q.key * scale + log_count and its value; prototypes
+ * are taken in node-slot order.  S == 0 is plain block-sparse attention.  The workspace
+ * (spruce_residual_workspace_bytes) holds the gathered summary keys in the compute dtype, padded to
+ * ceil(S * prototypes / 64) blocks of 64 per row. */
+SPRUCE_API int64_t spruce_residual_workspace_bytes(int64_t B, int64_t Hkv, int64_t T, int64_t D, int64_t S,
+                                                   int64_t prototypes, int dtype);
+SPRUCE_API int spruce_residual_sparse_attention_fwd(const void *q, const int64_t q_strides[4], const void *k,
+                                                    const int64_t k_strides[4], const void *v,
+                                                    const int64_t v_strides[4], const int32_t *indices,
+                                                    const int64_t idx_strides[4], const int32_t *nodes,
+                                                    const int64_t node_strides[4], int64_t S,
+                                                    const float *summary_keys, const float *summary_values,
+                                                    const float *summary_counts, const float *summary_log_counts,
+                                                    int64_t num_nodes, int64_t prototypes, void *out,
+                                                    const int64_t out_strides[4], int dtype, int64_t B, int64_t Hq,
+                                                    int64_t Hkv, int64_t T, int64_t D, int64_t Kw, float scale,
+                                                    void *workspace, int64_t workspace_bytes, uint32_t *status,
+                                                    void *stream);
+
 /*
  * build_kv_summary_table, sparse/summaries.py:52-142 (token ranges of
  * _prototype_token_ranges :29-49): for every node n of a residual tree

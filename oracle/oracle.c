@@ -412,6 +412,103 @@ void oracle_sparse_attention_rows(const float *q, const float *k, const float *v
 }
 
 /*
+ * Residual-summary attention, sparse/attention.py:178-265: per (b, g, query
+ * block i, head, token) the scores of the selected blocks' causal keys (as
+ * in oracle_sparse_attention_rows), then, for each residual node id
+ * nodes[b, g, i, s] >= 0 in order and each prototype p with
+ * counts[b, node, p] > 0, the summary score q.key * scale + log_counts[b,
+ * node, p] (no causal mask), one softmax over both (double sums) and the
+ * matching values.  Summary table: keys/values [B, Hkv, NN, P, D],
+ * counts/log_counts [B, NN, P]; nodes [B, Hkv, qb, S].
+ */
+void oracle_residual_attention(const float *q, const float *k, const float *v, const int32_t *idx,
+                               const int32_t *nodes, int64_t S, const float *skeys, const float *svalues,
+                               const float *scounts, const float *slogc, int64_t NN, int64_t P,
+                               int64_t B, int64_t Hq, int64_t Hkv, int64_t T, int64_t D, int64_t Kw,
+                               int64_t block, float scale, float *out) {
+    const int64_t qb = (T + block - 1) / block;
+    const int64_t rep = Hq / Hkv;
+    const int64_t cap = Kw * block + S * P + 1;
+#pragma omp parallel
+    {
+        /* key c: >= 0 a token of the sequence, < 0 summary row -(1 + s * P + p) */
+        int64_t *keys = (int64_t *)malloc(sizeof(int64_t) * (size_t)cap);
+        float *sc = (float *)malloc(sizeof(float) * (size_t)cap);
+        double *acc = (double *)malloc(sizeof(double) * (size_t)D);
+#pragma omp for schedule(dynamic, 1)
+        for (int64_t unit = 0; unit < B * Hkv * qb * rep; ++unit) {
+            const int64_t hh = unit % rep;
+            const int64_t b = unit / (Hkv * qb * rep);
+            const int64_t g = (unit / (qb * rep)) % Hkv;
+            const int64_t i = (unit / rep) % qb;
+            const int32_t *row = idx + (((size_t)b * Hkv + g) * qb + i) * Kw;
+            const int32_t *nrow = nodes + (((size_t)b * Hkv + g) * qb + i) * S;
+            int64_t nk = 0;
+            for (int64_t c = 0; c < Kw; ++c) {
+                if (row[c] < 0) continue;
+                for (int64_t t = 0; t < block; ++t) {
+                    int64_t key = (int64_t)row[c] * block + t;
+                    if (key < T) keys[nk++] = key;
+                }
+            }
+            for (int64_t s = 0; s < S; ++s) {
+                const int32_t node = nrow[s];
+                if (node < 0 || node >= NN) continue;
+                for (int64_t p = 0; p < P; ++p)
+                    if (scounts[((size_t)b * NN + node) * P + p] > 0.0f) keys[nk++] = -(1 + s * P + p);
+            }
+            const float *kg = k + ((size_t)b * Hkv + g) * T * D;
+            const float *vg = v + ((size_t)b * Hkv + g) * T * D;
+            const int64_t h = g * rep + hh;
+            for (int64_t t = i * block; t < (i + 1) * block && t < T; ++t) {
+                const float *qr = q + (((size_t)b * Hq + h) * T + t) * D;
+                float m = -INFINITY;
+                for (int64_t c = 0; c < nk; ++c) {
+                    const float *kr;
+                    float bias = 0.0f;
+                    if (keys[c] >= 0) {
+                        if (keys[c] > t) { sc[c] = -INFINITY; continue; }
+                        kr = kg + (size_t)keys[c] * D;
+                    } else {
+                        const int64_t e = -keys[c] - 1, node = nrow[e / P], p = e % P;
+                        kr = skeys + ((((size_t)b * Hkv + g) * NN + node) * P + p) * D;
+                        bias = slogc[((size_t)b * NN + node) * P + p];
+                    }
+                    float dot = 0.0f;
+                    for (int64_t d = 0; d < D; ++d) dot += qr[d] * kr[d];
+                    sc[c] = dot * scale + bias;
+                    if (sc[c] > m) m = sc[c];
+                }
+                float *o = out + (((size_t)b * T + t) * Hq + h) * D;
+                if (m == -INFINITY) {
+                    for (int64_t d = 0; d < D; ++d) o[d] = 0.0f;
+                    continue;
+                }
+                double l = 0.0;
+                for (int64_t d = 0; d < D; ++d) acc[d] = 0.0;
+                for (int64_t c = 0; c < nk; ++c) {
+                    if (sc[c] == -INFINITY) continue;
+                    const double pr = exp((double)sc[c] - (double)m);
+                    l += pr;
+                    const float *vr;
+                    if (keys[c] >= 0) {
+                        vr = vg + (size_t)keys[c] * D;
+                    } else {
+                        const int64_t e = -keys[c] - 1, node = nrow[e / P], p = e % P;
+                        vr = svalues + ((((size_t)b * Hkv + g) * NN + node) * P + p) * D;
+                    }
+                    for (int64_t d = 0; d < D; ++d) acc[d] += pr * (double)vr[d];
+                }
+                for (int64_t d = 0; d < D; ++d) o[d] = (float)(acc[d] / l);
+            }
+        }
+        free(keys);
+        free(sc);
+        free(acc);
+    }
+}
+
+/*
  * build_kv_summary_table, sparse/summaries.py:52-142, with the prototype
  * token ranges of _prototype_token_ranges (:29-49).
  *

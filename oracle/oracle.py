@@ -68,6 +68,8 @@ def lib():
         L.oracle_kv_summary_table.argtypes = [P, P, ctypes.c_int, P, I64, I64, I64, I64, I64, I64, P, P, I64,
                                               P, P, P, P, P, P]
         L.oracle_maxsim.argtypes = [P, P, P, I64, I64, I64, I64, I64, I64, P]
+        L.oracle_residual_attention.argtypes = [P, P, P, P, P, I64, P, P, P, P, I64, I64, I64, I64, I64, I64,
+                                                I64, I64, I64, F, P]
         L.oracle_num_threads.restype = ctypes.c_int
         _lib = L
     return _lib
@@ -235,6 +237,31 @@ def sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices:
     out = torch.zeros((B, T, Hq, D), dtype=torch.float32)
     lib().oracle_sparse_attention_rows(_ptr(qf), _ptr(kf), _ptr(vf), _ptr(idx), B, Hq, Hkv, T, D,
                                        idx.shape[-1], block, float(scale), i0, i1, _ptr(out))
+    return out.to(out_dtype or q.dtype)
+
+
+def residual_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices: torch.Tensor,
+                              nodes: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, counts: torch.Tensor,
+                              log_counts: torch.Tensor, scale: float | None = None, block: int = 64,
+                              out_dtype=None) -> torch.Tensor:
+    """Selected blocks plus residual summary keys in one softmax (sparse/attention.py:178-265).
+
+    indices int32 [B, Hkv, qb, K], nodes int32 [B, Hkv, qb, S]; summary keys/values
+    fp32 [B, Hkv, NN, P, D], counts/log_counts [B, NN, P].  Returns [B, T, Hq, D].
+    """
+    B, Hq, T, D = q.shape
+    Hkv = k.shape[1]
+    if scale is None:
+        scale = D ** -0.5
+    f = lambda x: x.detach().float().cpu().contiguous()  # noqa: E731
+    qf, kf, vf = f(q), f(k), f(v)
+    sk, sv, scnt, slc = f(keys), f(values), f(counts), f(log_counts)
+    idx = indices.detach().cpu().to(torch.int32).contiguous()
+    nd = nodes.detach().cpu().to(torch.int32).contiguous()
+    out = torch.zeros((B, T, Hq, D), dtype=torch.float32)
+    lib().oracle_residual_attention(_ptr(qf), _ptr(kf), _ptr(vf), _ptr(idx), _ptr(nd), nd.shape[-1], _ptr(sk),
+                                    _ptr(sv), _ptr(scnt), _ptr(slc), sk.shape[2], sk.shape[3], B, Hq, Hkv, T, D,
+                                    idx.shape[-1], block, float(scale), _ptr(out))
     return out.to(out_dtype or q.dtype)
 
 

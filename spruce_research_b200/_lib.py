@@ -56,6 +56,10 @@ SIGNATURES = {
     "spruce_kv_summary_workspace_bytes": ([_I64, _I64, _I64, _I64], _I64),
     "spruce_kv_summary_table": ([_P, _P, _P, _P, _P, _INT, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _I64,
                                  _P, _P, _P, _P, _P, _P, _P, _I64, _P], _INT),
+    "spruce_residual_workspace_bytes": ([_I64, _I64, _I64, _I64, _I64, _I64, _INT], _I64),
+    "spruce_residual_sparse_attention_fwd": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _P, _P, _P, _P, _I64,
+                                              _I64, _P, _P, _INT, _I64, _I64, _I64, _I64, _I64, _I64, _F, _P, _I64,
+                                              _P, _P], _INT),
     "spruce_ipc_export": ([_P, _P, ctypes.POINTER(ctypes.c_int64)], _INT),
     "spruce_ipc_import": ([_P, _I64, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p)], _INT),
     "spruce_ipc_close": ([_P], _INT),

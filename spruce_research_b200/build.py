@@ -19,7 +19,7 @@ REPO = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libspruce_b200.so")
 SOURCES = ["pool.cu", "select.cu", "tree.cu", "attn_sm100.cu", "attn_pair_sm100.cu", "attn_f32.cu",
-           "summaries.cu", "capi.cu"]
+           "summaries.cu", "residual.cu", "capi.cu"]
 HEADERS = ["common.cuh", "kernels.h", "attn_common.cuh"]
 
 NVCC_FLAGS = [

@@ -17,6 +17,9 @@ struct AttnParams {
   int q_begin, nq;  // query blocks [q_begin, q_begin + nq) are computed
   float scale_log2;
   uint32_t* status;
+  const float* vbias;     // residual summaries (see AttnArgs); nullptr: none
+  const int32_t* vcount;
+  int Tv, nvb;
 };
 
 // Output tensor maps: [0] this GPU's output, [1..] the peers' outputs for the
@@ -201,6 +204,10 @@ static inline AttnParams attn_params(const AttnArgs& a) {
   p.n_cta = (p.n_pair + 1) / 2;
   p.scale_log2 = a.scale * 1.4426950408889634f;
   p.status = a.status;
+  p.vbias = a.vbias;
+  p.vcount = a.vcount;
+  p.Tv = a.Tv;
+  p.nvb = a.nvb;
   return p;
 }
 

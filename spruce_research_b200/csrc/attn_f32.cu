@@ -7,6 +7,9 @@
 // column quarters, K/V tiles of the selected blocks staged in shared memory,
 // exact online softmax in fp32 (expf).  Same index semantics as the tcgen05
 // kernel: ids < 0 skipped, ids above the query block contribute nothing.
+// With residual summaries the row's virtual blocks (gathered summary keys,
+// sparse/attention.py:224-263) follow its selected blocks in the same online
+// softmax: score = q.k * scale + natural-log count bias, no causal mask.
 #include <algorithm>
 
 #include "common.cuh"
@@ -26,6 +29,12 @@ struct F32Params {
   int Hq, Hkv, T, Kw, qb, rep, q_begin, nq;
   float scale;
   uint32_t* status;
+  const float* vk;  // residual summaries (nullptr: none), see AttnArgs
+  const float* vv;
+  int64_t vksb, vksh, vkst, vvsb, vvsh, vvst;
+  const float* vbias;
+  const int32_t* vcount;
+  int Tv, nvb;
 };
 
 template <int D>
@@ -60,6 +69,8 @@ __global__ void __launch_bounds__(256) attn_fwd_f32_kernel(const F32Params p) {
     }
     if (lane == 0) nsel = count;
   }
+  __shared__ int nvirt;
+  if (tid == 0) nvirt = p.vk != nullptr ? min(p.vcount[((int64_t)b * p.Hkv + g) * p.qb + i], p.nvb) : 0;
   const int qtok0 = i * 64;
   for (int e = tid; e < 64 * D; e += 256) {
     const int rr = e / D, d = e % D;
@@ -68,6 +79,7 @@ __global__ void __launch_bounds__(256) attn_fwd_f32_kernel(const F32Params p) {
   }
   __syncthreads();
   const int n = nsel;
+  const int nv = nvirt;
 
   constexpr int DQ = D / 4;
   float o[DQ];
@@ -76,18 +88,28 @@ __global__ void __launch_bounds__(256) attn_fwd_f32_kernel(const F32Params p) {
   float m = -INFINITY, l = 0.0f;
   const int qtok = qtok0 + r;
 
-  for (int j = 0; j < n; ++j) {
-    const int blk = ids[j];
-    const int k0 = blk * 64;
+  for (int j = 0; j < n + nv; ++j) {
+    const bool virt = j >= n;  // a virtual block of summary keys
+    const int k0 = virt ? (i * p.nvb + (j - n)) * 64 : ids[j] * 64;
     __syncthreads();
-    for (int e = tid; e < 64 * D; e += 256) {
-      const int rr = e / D, d = e % D;
-      const int t = k0 + rr;
-      const bool in = t < p.T;
-      Ks[rr * KP + d] = in ? p.k[b * p.ksb + g * p.ksh + (int64_t)t * p.kst + d] : 0.0f;
-      Vs[rr * D + d] = in ? p.v[b * p.vsb + g * p.vsh + (int64_t)t * p.vst + d] : 0.0f;
+    if (!virt) {
+      for (int e = tid; e < 64 * D; e += 256) {
+        const int rr = e / D, d = e % D;
+        const int t = k0 + rr;
+        const bool in = t < p.T;
+        Ks[rr * KP + d] = in ? p.k[b * p.ksb + g * p.ksh + (int64_t)t * p.kst + d] : 0.0f;
+        Vs[rr * D + d] = in ? p.v[b * p.vsb + g * p.vsh + (int64_t)t * p.vst + d] : 0.0f;
+      }
+    } else {
+      for (int e = tid; e < 64 * D; e += 256) {
+        const int rr = e / D, d = e % D;
+        const int64_t t = k0 + rr;
+        Ks[rr * KP + d] = p.vk[b * p.vksb + g * p.vksh + t * p.vkst + d];
+        Vs[rr * D + d] = p.vv[b * p.vvsb + g * p.vvsh + t * p.vvst + d];
+      }
     }
     __syncthreads();
+    const float* vbias = virt ? p.vbias + ((int64_t)b * p.Hkv + g) * p.Tv + k0 : nullptr;
     float s[16];
     float mx = -INFINITY;
 #pragma unroll
@@ -105,7 +127,10 @@ __global__ void __launch_bounds__(256) attn_fwd_f32_kernel(const F32Params p) {
         acc = fmaf(x.w, y.w, acc);
       }
       float sc = acc * p.scale;
-      if (k0 + col > qtok) sc = -INFINITY;  // causal (also drops keys >= T for real rows)
+      if (virt)
+        sc += vbias[col];  // padding rows carry -inf
+      else if (k0 + col > qtok)
+        sc = -INFINITY;  // causal (also drops keys >= T for real rows)
       s[cc] = sc;
       mx = fmaxf(mx, sc);
     }
@@ -164,6 +189,18 @@ static cudaError_t launch_f32_typed(const AttnArgs& a, cudaStream_t stream) {
   p.nq = a.q_end - a.q_begin;
   p.scale = a.scale;
   p.status = a.status;
+  p.vk = static_cast<const float*>(a.vk);
+  p.vv = static_cast<const float*>(a.vv);
+  if (a.vk != nullptr) {
+    p.vksb = a.vks[0]; p.vksh = a.vks[1]; p.vkst = a.vks[2];
+    p.vvsb = a.vvs[0]; p.vvsh = a.vvs[1]; p.vvst = a.vvs[2];
+  } else {
+    p.vksb = p.vksh = p.vkst = p.vvsb = p.vvsh = p.vvst = 0;
+  }
+  p.vbias = a.vbias;
+  p.vcount = a.vcount;
+  p.Tv = a.Tv;
+  p.nvb = a.nvb;
   const size_t smem = sizeof(float) * (64 * D + 64 * (D + 4) + 64 * D + 64 * 65) + sizeof(int) * (size_t)a.Kw;
   cudaError_t e = cudaFuncSetAttribute(attn_fwd_f32_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;

@@ -39,6 +39,16 @@
 // 16 at a time.  O is rescaled only when the running max grows by more than 8
 // (log2 units).
 //
+// Residual summaries (SUM = true, sparse/attention.py:164-265): after its
+// selected blocks, a row takes its virtual blocks -- 64 gathered summary keys
+// each, read through a second pair of tensor maps -- as ordinary block slots
+// with ids kVirtualBase + i*nvb + j.  The producer stages each virtual half's
+// 64 count biases (natural log, times log2(e)) in shared memory before it
+// releases the stage's K barrier.  A pair with a virtual half moves all its
+// scores into log2 units first (scale*log2(e)*s, plus the bias where virtual;
+// no causal mask there), so the one online softmax covers blocks and
+// summaries exactly as the reference's concatenated scores.
+//
 // Warp roles (320 threads):
 //   warps 0-3  softmax + epilogue of tile 0 (TMEM lanes 0-127); warps 4-7 tile 1
 //   warp  8    TMA producer (Q once, then K/V of each block pair, STAGES ring)
@@ -71,17 +81,19 @@ struct PairLayout {
   // q_full, k_full[S], v_full[S], kv_empty[S], s_full[2], p_full[2][2], o_done[2], drain[2]
   static constexpr int NBAR = 1 + 3 * STAGES + 2 + 4 + 2 + 2;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
-  static constexpr int OFF_IDS = OFF_MISC + 16;
+  static constexpr int OFF_VB = (OFF_MISC + 16 + 15) / 16 * 16;  // [STAGES][128] fp32 virtual-key biases
+  static constexpr int OFF_IDS = OFF_VB + STAGES * 128 * 4;
   static constexpr int COL_S = 2 * D;  // S_t (and P_t) at COL_S + 128 t
   static constexpr uint32_t TMEM_COLS = 512u;
   static_assert(2 * D + 256 <= 512, "O and S of both tiles must fit in 512 TMEM columns");
   static size_t smem_bytes(int kw) { return 1024 + OFF_IDS + 4 * (size_t)kw; }
 };
 
-template <typename T, int D, int STAGES>
+template <typename T, int D, int STAGES, bool SUM>
 __global__ void __launch_bounds__(kPairThreads, 1)
     attn_pair_sm100_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
-                           const __grid_constant__ CUtensorMap tmv, const __grid_constant__ OutMaps om,
+                           const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmvk,
+                           const __grid_constant__ CUtensorMap tmvv, const __grid_constant__ OutMaps om,
                            const AttnParams p) {
   using L = PairLayout<D, STAGES>;
   extern __shared__ uint8_t smem_raw[];
@@ -121,6 +133,11 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       const unsigned m = __ballot_sync(0xffffffffu, keep);
       if (keep) ids[count + __popc(m & ((1u << lane) - 1u))] = id;
       count += __popc(m);
+    }
+    if constexpr (SUM) {  // then the row's virtual summary blocks
+      const int vc = min(p.vcount[((int64_t)b * p.Hkv + g) * p.qb + i], p.nvb);
+      for (int j = lane; j < vc; j += 32) ids[count + j] = kVirtualBase + i * p.nvb + j;
+      count += vc;
     }
     if (lane == 0) {
       *nsel_slot = count;
@@ -176,17 +193,34 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         if (j >= STAGES &&
             !__all_sync(0xffffffffu, mbar_wait(&kv_empty[st], ((j / STAGES) - 1) & 1, p.status, abort_flag)))
           break;
+        if constexpr (SUM) {
+          // Virtual halves' biases into this stage (released with k_full below).
+          float* vb = reinterpret_cast<float*>(smem + L::OFF_VB) + st * 128;
+          for (int h = 0; h < 2; ++h) {
+            const int id = ids[min(2 * j + h, n - 1)];
+            if (id >= kVirtualBase) {
+              const float* src = p.vbias + ((int64_t)b * p.Hkv + g) * p.Tv + (int64_t)(id - kVirtualBase) * 64;
+              vb[h * 64 + lane] = src[lane] * 1.4426950408889634f;
+              vb[h * 64 + 32 + lane] = src[32 + lane] * 1.4426950408889634f;
+            }
+          }
+          __syncwarp();
+        }
         if (leader) {
           uint8_t* ks = smem + L::OFF_K + st * L::KV_TILE;
           uint8_t* vs = smem + L::OFF_V + st * L::KV_TILE;
           mbar_arrive_expect_tx(&k_full[st], L::KV_TILE);
           mbar_arrive_expect_tx(&v_full[st], L::KV_TILE);
           for (int h = 0; h < 2; ++h) {
-            const int tok = ids[min(2 * j + h, n - 1)] * 64;
+            const int id = ids[min(2 * j + h, n - 1)];
+            const bool virt = SUM && id >= kVirtualBase;
+            const int tok = (virt ? id - kVirtualBase : id) * 64;
+            const CUtensorMap* mk = virt ? &tmvk : &tmk;
+            const CUtensorMap* mv = virt ? &tmvv : &tmv;
             for (int pp = 0; pp < L::NP; ++pp)
-              tma_load_4d(ks + pp * L::KV_PANEL + h * L::HALF, &tmk, &k_full[st], pp * 64, g, tok, b);
+              tma_load_4d(ks + pp * L::KV_PANEL + h * L::HALF, mk, &k_full[st], pp * 64, g, tok, b);
             for (int pp = 0; pp < L::NP; ++pp)
-              tma_load_4d(vs + pp * L::KV_PANEL + h * L::HALF, &tmv, &v_full[st], pp * 64, g, tok, b);
+              tma_load_4d(vs + pp * L::KV_PANEL + h * L::HALF, mv, &v_full[st], pp * 64, g, tok, b);
           }
         }
         __syncwarp();
@@ -310,6 +344,36 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 #pragma unroll
         for (int q = 0; q < 4; ++q) tmem_ld32(tS + 32 * q, s[q]);
         tmem_wait_ld();
+        // A pair with a virtual (summary) half: every score to log2 units now,
+        // plus the count bias on the virtual half; the scaling below is then 1.
+        float sl = sl2;
+        if constexpr (SUM) {
+          const bool v0 = ids[2 * j] >= kVirtualBase;
+          const bool v1 = !dup1 && ids[2 * j + 1] >= kVirtualBase;
+          if (v0 || v1) {  // warp-uniform
+            // the producer's bias stores are visible once this stage's K phase has completed
+            ok = __all_sync(0xffffffffu, mbar_wait(&k_full[j % STAGES], (j / STAGES) & 1, p.status, abort_flag));
+            if (!ok) break;
+            const float* vb = reinterpret_cast<const float*>(smem + L::OFF_VB) + (j % STAGES) * 128;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              if (q < 2 ? v0 : v1) {
+#pragma unroll
+                for (int c4 = 0; c4 < 8; ++c4) {
+                  const float4 w = *reinterpret_cast<const float4*>(vb + 32 * q + 4 * c4);
+                  s[q][4 * c4 + 0] = fmaf(s[q][4 * c4 + 0], sl2, w.x);
+                  s[q][4 * c4 + 1] = fmaf(s[q][4 * c4 + 1], sl2, w.y);
+                  s[q][4 * c4 + 2] = fmaf(s[q][4 * c4 + 2], sl2, w.z);
+                  s[q][4 * c4 + 3] = fmaf(s[q][4 * c4 + 3], sl2, w.w);
+                }
+              } else {
+#pragma unroll
+                for (int c = 0; c < 32; ++c) s[q][c] *= sl2;
+              }
+            }
+            sl = 1.0f;
+          }
+        }
         // The reference's masks: the diagonal block keeps keys <= the row's token,
         // the repeated odd block none.
         if (dup1 || diag0 || diag1) {  // warp-uniform: only the diagonal pair and an odd last pair
@@ -336,7 +400,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           mx8[u] = fmaxf(a, s[3][u + 24]);
         }
         const float mx = fmaxf(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], fmax3(mx8[5], mx8[6], mx8[7])));
-        const float m_new = fmaxf(m_used, mx * sl2);
+        const float m_new = fmaxf(m_used, mx * sl);
         const bool rescale = (j == 0) || (m_new > m_used + 8.0f);
         const float alpha = (j > 0 && rescale) ? fast_exp2(m_used - m_new) : 1.0f;
         if (rescale) m_used = m_new;
@@ -344,7 +408,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         // Exponentials -> P over S_t's first 64 columns, 16 columns per store.
         float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
         uint64_t sum2[2] = {f2_pack(0.0f, 0.0f), f2_pack(0.0f, 0.0f)};
-        const uint64_t sl2x2 = f2_pack(sl2, sl2), nref2 = f2_pack(neg_ref, neg_ref);
+        const uint64_t sl2x2 = f2_pack(sl, sl), nref2 = f2_pack(neg_ref, neg_ref);
         const bool any_diag = diag0 || diag1;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -464,20 +528,29 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 template <typename T, int D, int STAGES>
 static cudaError_t launch_pair_typed(const AttnArgs& a, CUtensorMapDataType dt, cudaStream_t stream) {
   using L = PairLayout<D, STAGES>;
-  CUtensorMap tmq, tmk, tmv;
+  CUtensorMap tmq, tmk, tmv, tmvk, tmvv;
   if (!make_map(&tmq, a.q, dt, a.B, a.Hq, a.T, D, a.qs, 2) || !make_map(&tmk, a.k, dt, a.B, a.Hkv, a.T, D, a.ks, 1) ||
       !make_map(&tmv, a.v, dt, a.B, a.Hkv, a.T, D, a.vs, 1))
     return cudaErrorInvalidValue;
+  const bool sum = a.vk != nullptr;
+  if (sum) {
+    if (!make_map(&tmvk, a.vk, dt, a.B, a.Hkv, a.Tv, D, a.vks, 1) ||
+        !make_map(&tmvv, a.vv, dt, a.B, a.Hkv, a.Tv, D, a.vvs, 1))
+      return cudaErrorInvalidValue;
+  } else {
+    tmvk = tmk;
+    tmvv = tmv;
+  }
   const AttnParams p = attn_params(a);
   OutMaps om;
   if (!attn_out_maps(a, dt, D, &om)) return cudaErrorInvalidValue;
-  const size_t smem = L::smem_bytes(a.Kw);
-  auto kern = attn_pair_sm100_kernel<T, D, STAGES>;
+  const size_t smem = L::smem_bytes(a.Kw + (sum ? a.nvb : 0));
+  auto kern = sum ? attn_pair_sm100_kernel<T, D, STAGES, true> : attn_pair_sm100_kernel<T, D, STAGES, false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   if (p.nq <= 0) return cudaSuccess;
   dim3 grid(p.nq * p.n_cta, a.Hkv, a.B);
-  kern<<<grid, kPairThreads, smem, stream>>>(tmq, tmk, tmv, om, p);
+  kern<<<grid, kPairThreads, smem, stream>>>(tmq, tmk, tmv, tmvk, tmvv, om, p);
   return cudaGetLastError();
 }
 
@@ -489,7 +562,7 @@ int attn_pair_max_kw(int D) {
 }
 
 cudaError_t launch_attn_pair(const AttnArgs& a, int dtype, cudaStream_t stream) {
-  if (a.Kw > attn_pair_max_kw(a.D)) return cudaErrorInvalidValue;
+  if (a.Kw + (a.vk != nullptr ? a.nvb : 0) > attn_pair_max_kw(a.D)) return cudaErrorInvalidValue;
   if (dtype == SPRUCE_DTYPE_BF16) {
     if (a.D == 128) return launch_pair_typed<__nv_bfloat16, 128, 2>(a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, stream);
     if (a.D == 64) return launch_pair_typed<__nv_bfloat16, 64, 4>(a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, stream);

@@ -485,7 +485,8 @@ static bool use_single_block_kernel() {
 }
 
 cudaError_t launch_attn_sm100(const AttnArgs& a, int dtype, cudaStream_t stream) {
-  if (!use_single_block_kernel()) return launch_attn_pair(a, dtype, stream);
+  // residual summaries are served by the pair kernel only
+  if (!use_single_block_kernel() || a.vk != nullptr) return launch_attn_pair(a, dtype, stream);
   if (a.Kw > attn_sm100_max_kw(a.D)) return cudaErrorInvalidValue;
   if (dtype == SPRUCE_DTYPE_BF16) {
     if (a.D == 128) return launch_typed<__nv_bfloat16, 128, 4>(a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, stream);

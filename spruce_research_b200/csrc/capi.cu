@@ -61,7 +61,7 @@ static int spruce_sparse_attention_fwd_rows_impl(const void* q, const int64_t q_
                                                  int64_t Hkv, int64_t T, int64_t D, int64_t Kw, float scale,
                                                  int64_t q_block_begin, int64_t q_block_end,
                                                  const void* const* peer_outs, int n_peers, uint32_t* status,
-                                                 void* stream);
+                                                 void* stream, const spruce::AttnArgs* virt = nullptr);
 
 const char* spruce_last_error(void) { return g_last_error.c_str(); }
 
@@ -521,7 +521,7 @@ static int spruce_sparse_attention_fwd_rows_impl(const void* q, const int64_t q_
                                      const int64_t out_strides[4], int dtype, int64_t B, int64_t Hq, int64_t Hkv,
                                      int64_t T, int64_t D, int64_t Kw, float scale, int64_t q_block_begin,
                                      int64_t q_block_end, const void* const* peer_outs, int n_peers,
-                                     uint32_t* status, void* stream) {
+                                     uint32_t* status, void* stream, const spruce::AttnArgs* virt) {
   if (!valid_dtype(dtype)) return fail(SPRUCE_ERR_INVALID, "unsupported dtype code %d", dtype);
   if (D != 64 && D != 128) return fail(SPRUCE_ERR_INVALID, "kernel supports head_dim 64 or 128, got %lld", (long long)D);
   if (B < 0 || Hq < 1 || Hkv < 1 || T < 0 || Kw < 0) return fail(SPRUCE_ERR_INVALID, "bad attention shape");
@@ -538,6 +538,16 @@ static int spruce_sparse_attention_fwd_rows_impl(const void* q, const int64_t q_
   spruce::AttnArgs a{q, k, v, q_strides, k_strides, v_strides, indices, idx_strides, out, out_strides,
                      (int)B, (int)Hq, (int)Hkv, (int)T, (int)D, (int)Kw, scale, status,
                      (int)q_block_begin, (int)q_block_end, peer_outs, n_peers};
+  if (virt != nullptr) {  // residual summaries: the gathered virtual K/V of every row
+    a.vk = virt->vk;
+    a.vv = virt->vv;
+    a.vks = virt->vks;
+    a.vvs = virt->vvs;
+    a.vbias = virt->vbias;
+    a.vcount = virt->vcount;
+    a.Tv = virt->Tv;
+    a.nvb = virt->nvb;
+  }
   if (dtype == SPRUCE_DTYPE_F32) {
     if (Kw > 8192) return fail(SPRUCE_ERR_UNSUPPORTED, "row width %lld too large", (long long)Kw);
     return cuda_status(spruce::launch_attn_f32(a, as_stream(stream)), "fp32 attention launch");
@@ -551,8 +561,10 @@ static int spruce_sparse_attention_fwd_rows_impl(const void* q, const int64_t q_
   }
   if (!aligned16(out) || out_strides[0] % 8 || out_strides[1] % 8 || out_strides[2] % 8)
     return fail(SPRUCE_ERR_UNSUPPORTED, "out needs 16-byte aligned base and strides");
-  if (Kw > spruce::attn_sm100_max_kw((int)D))
-    return fail(SPRUCE_ERR_UNSUPPORTED, "row width %lld exceeds %d", (long long)Kw, spruce::attn_sm100_max_kw((int)D));
+  const int64_t kw_all = Kw + (virt != nullptr ? virt->nvb : 0);
+  if (kw_all > spruce::attn_sm100_max_kw((int)D))
+    return fail(SPRUCE_ERR_UNSUPPORTED, "row width %lld exceeds %d", (long long)kw_all,
+                spruce::attn_sm100_max_kw((int)D));
   return cuda_status(spruce::launch_attn_sm100(a, dtype, as_stream(stream)), "tcgen05 attention launch");
 }
 
@@ -565,6 +577,86 @@ int spruce_sparse_attention_fwd(const void* q, const int64_t q_strides[4], const
   return spruce_sparse_attention_fwd_rows(q, q_strides, k, k_strides, v, v_strides, indices, idx_strides, out,
                                           out_strides, dtype, B, Hq, Hkv, T, D, Kw, scale, 0, qb < 0 ? 0 : qb,
                                           status, stream);
+}
+
+// Workspace of the residual-summary attention: virtual K and V in the compute
+// dtype, their fp32 biases and the per-row virtual block counts.
+struct ResidualWorkspace {
+  int64_t nvb, Tv, off_vv, off_bias, off_count, total;
+};
+
+static ResidualWorkspace residual_workspace(int64_t B, int64_t Hkv, int64_t T, int64_t D, int64_t S, int64_t P,
+                                            int dtype) {
+  auto up = [](int64_t x) { return (x + 255) / 256 * 256; };
+  ResidualWorkspace w;
+  const int64_t qb = (T + SPRUCE_BLOCK - 1) / SPRUCE_BLOCK;
+  w.nvb = (S * P + SPRUCE_BLOCK - 1) / SPRUCE_BLOCK;
+  w.Tv = qb * w.nvb * SPRUCE_BLOCK;
+  const int64_t kv = up(B * Hkv * w.Tv * D * elem_size(dtype));
+  w.off_vv = kv;
+  w.off_bias = 2 * kv;
+  w.off_count = w.off_bias + up(B * Hkv * w.Tv * 4);
+  w.total = w.off_count + up(B * Hkv * qb * 4);
+  return w;
+}
+
+int64_t spruce_residual_workspace_bytes(int64_t B, int64_t Hkv, int64_t T, int64_t D, int64_t S, int64_t prototypes,
+                                        int dtype) {
+  if (B < 0 || Hkv < 0 || T < 0 || D < 1 || S < 0 || prototypes < 1 || !valid_dtype(dtype)) return -1;
+  return residual_workspace(B, Hkv, T, D, S, prototypes, dtype).total;
+}
+
+int spruce_residual_sparse_attention_fwd(const void* q, const int64_t q_strides[4], const void* k,
+                                         const int64_t k_strides[4], const void* v, const int64_t v_strides[4],
+                                         const int32_t* indices, const int64_t idx_strides[4], const int32_t* nodes,
+                                         const int64_t node_strides[4], int64_t S, const float* summary_keys,
+                                         const float* summary_values, const float* summary_counts,
+                                         const float* summary_log_counts, int64_t num_nodes, int64_t prototypes,
+                                         void* out, const int64_t out_strides[4], int dtype, int64_t B, int64_t Hq,
+                                         int64_t Hkv, int64_t T, int64_t D, int64_t Kw, float scale, void* workspace,
+                                         int64_t workspace_bytes, uint32_t* status, void* stream) {
+  if (!valid_dtype(dtype)) return fail(SPRUCE_ERR_INVALID, "unsupported dtype code %d", dtype);
+  if (S < 0 || prototypes < 1 || prototypes > 64 || num_nodes < 0)
+    return fail(SPRUCE_ERR_INVALID, "bad residual summary shape (S=%lld, prototypes=%lld, nodes=%lld)", (long long)S,
+                (long long)prototypes, (long long)num_nodes);
+  const int64_t qb = (T + SPRUCE_BLOCK - 1) / SPRUCE_BLOCK;
+  if (S == 0 || B == 0 || T == 0)  // no residual node anywhere: plain block-sparse attention
+    return spruce_sparse_attention_fwd_rows_impl(q, q_strides, k, k_strides, v, v_strides, indices, idx_strides, out,
+                                                 out_strides, dtype, B, Hq, Hkv, T, D, Kw, scale, 0, qb, nullptr, 0,
+                                                 status, stream);
+  if (nodes == nullptr || summary_keys == nullptr || summary_values == nullptr || summary_counts == nullptr ||
+      summary_log_counts == nullptr)
+    return fail(SPRUCE_ERR_INVALID, "residual summaries need nodes and the summary table");
+  if (S * prototypes > 51200)
+    return fail(SPRUCE_ERR_UNSUPPORTED, "residual width %lld x %lld prototypes too large", (long long)S,
+                (long long)prototypes);
+  if (Hkv > 65535 || B > 65535 || qb > 65535 * 64) return fail(SPRUCE_ERR_UNSUPPORTED, "shape too large");
+  const ResidualWorkspace w = residual_workspace(B, Hkv, T, D, S, prototypes, dtype);
+  if (w.Tv > ((int64_t)1 << 31) - 64) return fail(SPRUCE_ERR_UNSUPPORTED, "too many residual summary keys");
+  if (workspace == nullptr || workspace_bytes < w.total)
+    return fail(SPRUCE_ERR_WORKSPACE, "residual workspace needs %lld bytes, got %lld", (long long)w.total,
+                (long long)workspace_bytes);
+  if (!aligned16(workspace)) return fail(SPRUCE_ERR_UNSUPPORTED, "workspace must be 16-byte aligned");
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  spruce::ResidualGatherArgs g{nodes, {node_strides[0], node_strides[1], node_strides[2], node_strides[3]}, (int)S,
+                               summary_keys, summary_values, summary_counts, summary_log_counts, (int)num_nodes,
+                               (int)prototypes, (int)B, (int)Hkv, (int)qb, (int)D, (int)w.nvb, ws, ws + w.off_vv,
+                               reinterpret_cast<float*>(ws + w.off_bias), reinterpret_cast<int32_t*>(ws + w.off_count)};
+  int rc = cuda_status(spruce::launch_residual_gather(g, dtype, as_stream(stream)), "residual gather launch");
+  if (rc != SPRUCE_OK) return rc;
+  const int64_t vstr[4] = {Hkv * w.Tv * D, w.Tv * D, D, 1};
+  spruce::AttnArgs virt{};
+  virt.vk = ws;
+  virt.vv = ws + w.off_vv;
+  virt.vks = vstr;
+  virt.vvs = vstr;
+  virt.vbias = reinterpret_cast<const float*>(ws + w.off_bias);
+  virt.vcount = reinterpret_cast<const int32_t*>(ws + w.off_count);
+  virt.Tv = (int)w.Tv;
+  virt.nvb = (int)w.nvb;
+  return spruce_sparse_attention_fwd_rows_impl(q, q_strides, k, k_strides, v, v_strides, indices, idx_strides, out,
+                                               out_strides, dtype, B, Hq, Hkv, T, D, Kw, scale, 0, qb, nullptr, 0,
+                                               status, stream, &virt);
 }
 
 int64_t spruce_kv_summary_workspace_bytes(int64_t B, int64_t Hkv, int64_t T, int64_t D) {

@@ -70,9 +70,45 @@ struct AttnArgs {
   // offset in each of these peer buffers (P2P-mapped, identical layout).
   const void* const* peer_out;
   int n_peer;
+  // Residual summaries (optional; vk == nullptr: none).  Row (b, g, i) also
+  // attends to vcount[(b*Hkv + g)*qb + i] virtual blocks of 64 gathered
+  // summary keys: virtual tokens [i*nvb*64, ...) of vk / vv ([B, Hkv, Tv, D],
+  // element strides vks / vvs), each with the additive natural-log count bias
+  // vbias[(b*Hkv + g)*Tv + token] and no causal mask.
+  const void* vk;
+  const void* vv;
+  const int64_t* vks;
+  const int64_t* vvs;
+  const float* vbias;
+  const int32_t* vcount;
+  int Tv, nvb;
 };
 
+// Virtual block ids start here in a row's compacted id list.
+constexpr int kVirtualBase = 1 << 30;
+
 constexpr int kMaxPeers = 7;
+
+// Residual-summary gather: each row's valid (count > 0) node prototypes, in
+// node-then-prototype order, become rows of the virtual K/V (in the compute
+// dtype) with their natural-log count bias; rows up to the next multiple of 64
+// are zero with bias -inf.  vcount receives the row's virtual block count.
+struct ResidualGatherArgs {
+  const int32_t* nodes;   // [B, Hkv, qb, S] residual node ids (-1 padded)
+  int64_t ns[4];          // their element strides (by value: read on the device)
+  int S;
+  const float* keys;      // [B, Hkv, NN, P, D] summary table
+  const float* values;
+  const float* counts;    // [B, NN, P]
+  const float* log_counts;
+  int NN, P;
+  int B, Hkv, qb, D, nvb;
+  void* vk;               // [B, Hkv, qb*nvb*64, D]
+  void* vv;
+  float* vbias;           // [B, Hkv, qb*nvb*64]
+  int32_t* vcount;        // [B, Hkv, qb]
+};
+cudaError_t launch_residual_gather(const ResidualGatherArgs& a, int dtype, cudaStream_t stream);
 
 // tcgen05 path (bf16 / fp16).  Returns cudaErrorInvalidValue for shapes it
 // does not cover (the C ABI checks them first).

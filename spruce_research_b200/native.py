@@ -272,6 +272,55 @@ def sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices:
     return out
 
 
+def residual_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices: torch.Tensor,
+                              nodes: torch.Tensor, table, scale: float | None = None,
+                              out: torch.Tensor | None = None, status: torch.Tensor | None = None,
+                              workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Block-sparse attention whose softmax also covers each row's residual summary keys
+    (sparse/attention.py:164-265) -> token-major [B, T, Hq, D].
+
+    ``nodes`` int32 [B, Hkv, qb, S] residual node ids (-1 padded); ``table`` a
+    KVSummaryTable of the same K/V (keys/values fp32 [B, Hkv, nodes, P, D],
+    counts/log_counts fp32 [B, nodes, P]).
+    """
+    _lib.require_cuda(q, k, v, indices, nodes)
+    B, Hq, T, D = q.shape
+    Hkv = k.shape[1]
+    if scale is None:
+        scale = D ** -0.5
+    if not (q.dtype == k.dtype == v.dtype):
+        raise ValueError("q, k and v must share a dtype")
+    qb = (T + BLOCK - 1) // BLOCK
+    if indices.dtype != torch.int32 or tuple(indices.shape[:3]) != (B, Hkv, qb):
+        raise ValueError("indices must be int32 [B,Hkv,ceil(T/64),K]")
+    if nodes.dtype != torch.int32 or nodes.dim() != 4 or tuple(nodes.shape[:3]) != (B, Hkv, qb):
+        raise ValueError(f"residual nodes must be int32 [{B},{Hkv},{qb},S], got {tuple(nodes.shape)}")
+    keys, values = table.keys.float().contiguous(), table.values.float().contiguous()
+    counts, log_counts = table.counts.float().contiguous(), table.log_counts.float().contiguous()
+    NN, P = keys.shape[2], keys.shape[3]
+    if keys.shape != (B, Hkv, NN, P, D) or values.shape != keys.shape or counts.shape != (B, NN, P) \
+            or log_counts.shape != counts.shape:
+        raise ValueError("summary table shapes do not match q/k/v")
+    _lib.require_cuda(keys, values, counts, log_counts)
+    S = nodes.shape[3]
+    if out is None:
+        out = torch.empty((B, T, Hq, D), device=q.device, dtype=q.dtype)
+    ostr = _lib.int64s(out.stride(0), out.stride(2), out.stride(1), out.stride(3))
+    L = _lib.load()
+    need = L.spruce_residual_workspace_bytes(B, Hkv, T, D, S, P, _dt(q))
+    if need < 0:
+        raise ValueError("bad residual attention shape")
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(need, 16), device=q.device, dtype=torch.uint8)
+    _lib.check(L.spruce_residual_sparse_attention_fwd(
+        q.data_ptr(), _lib.strides(q), k.data_ptr(), _lib.strides(k), v.data_ptr(), _lib.strides(v),
+        indices.data_ptr(), _lib.strides(indices), nodes.data_ptr(), _lib.strides(nodes), S, keys.data_ptr(),
+        values.data_ptr(), counts.data_ptr(), log_counts.data_ptr(), NN, P, out.data_ptr(), ostr, _dt(q), B, Hq,
+        Hkv, T, D, indices.shape[-1], float(scale), workspace.data_ptr(), workspace.numel(),
+        status.data_ptr() if status is not None else None, _lib.stream_of(q)))
+    return out
+
+
 def gate_denominator(proj_dim: int) -> float:
     return float(math.sqrt(proj_dim))
 

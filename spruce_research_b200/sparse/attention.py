@@ -4,9 +4,12 @@ Mirrors sparse/attention.py:83-291 of the reference (the torch "correctness"
 backend): same keyword interface, input checks and error messages, the
 ``selected_blocks`` validator, and the token-major ``[B, T, Hq, D]`` output.
 Differences, all raised as errors rather than silently changed results:
-block_size must be 64 (the kernels' tile), the HF additive mask must be None
-(the kernel applies the causal mask itself), and residual summaries are not
-built on this path.  Shape errors are reported before row-rule errors.
+block_size must be 64 (the kernels' tile) and the HF additive mask must be
+None (the kernel applies the causal mask itself).  Shape errors are reported
+before row-rule errors.  With ``residual_summaries=True`` the K/V summary table
+is built on the GPU (sparse/summaries.py:52-142) and each row's softmax also
+covers its residual nodes' summary keys with the log-count bias
+(sparse/attention.py:164-265), in the same kernel launch as the selected blocks.
 """
 from __future__ import annotations
 
@@ -16,7 +19,9 @@ from typing import Optional
 import torch
 
 from .. import native
+from ..interfaces.residual_summaries import build_residual_tree_layout, validate_residual_summary_nodes
 from ..interfaces.validator import validate_selected_blocks
+from .summaries import build_kv_summary_table
 
 SPARSE_PREFILL_ATTENTION = "spruce_sparse_prefill"
 SUMMARY_PROTOTYPES = (1, 2, 4)
@@ -71,15 +76,25 @@ def sparse_prefill_attention_forward(module: torch.nn.Module, query: torch.Tenso
                                      validate_residual_summary_nodes_input: bool = True,
                                      **kwargs) -> tuple[torch.Tensor, None]:
     """AttentionInterface implementation for sparse prefill (sparse/attention.py:83-274)."""
-    del kwargs, residual_summary_nodes, summary_checkpoint, validate_residual_summary_nodes_input
+    del kwargs
     layer_idx = _layer_index(module)
     _validate_inputs(query, key, value, selected_blocks, block_size, layer_idx)
     if summary_prototypes not in SUMMARY_PROTOTYPES:
         raise ValueError(f"summary_prototypes must be one of {SUMMARY_PROTOTYPES}, got {summary_prototypes}")
     if summary_mode not in SUMMARY_MODES:
         raise ValueError(f"summary_mode must be one of {SUMMARY_MODES}, got {summary_mode!r}")
-    if residual_summaries:
-        raise NotImplementedError("residual-summary attention is not built on the B200 path")
+    if residual_summaries:  # the checks of sparse/attention.py:122-141, in order
+        if residual_summary_nodes is None:
+            raise ValueError("residual_summaries=True requires residual_summary_nodes; "
+                             "construct the complete frontier before model forward")
+        if summary_mode == "learned":
+            if not summary_checkpoint:
+                raise ValueError("summary_mode='learned' requires summary_checkpoint")
+            raise NotImplementedError("The learned compressor is gated on deterministic-summary "
+                                      "evaluation and is not implemented before that gate passes.")
+        if validate_residual_summary_nodes_input:
+            validate_residual_summary_nodes(selected_blocks, residual_summary_nodes,
+                                            validate_selected=not validate_selected_blocks_input)
     if block_size != 64:
         raise ValueError(f"the B200 kernels use 64-token blocks, got block_size={block_size}")
     if attention_mask is not None:
@@ -93,7 +108,14 @@ def sparse_prefill_attention_forward(module: torch.nn.Module, query: torch.Tenso
     indices = selected_blocks[:, layer_idx].to(device=query.device, dtype=torch.int32)
     if indices.stride(-1) != 1:
         indices = indices.contiguous()
-    out = native.sparse_attention(query, key, value, indices, scale=1.0 / math.sqrt(D))
+    if not residual_summaries:
+        return native.sparse_attention(query, key, value, indices, scale=1.0 / math.sqrt(D)), None
+    if residual_summary_nodes.shape[:4] != selected_blocks.shape[:4]:
+        raise ValueError("residual_summary_nodes must match selected_blocks through the query-block dimension")
+    nodes = residual_summary_nodes[:, layer_idx].to(device=query.device, dtype=torch.int32)
+    layout = build_residual_tree_layout(selected_blocks.shape[3])
+    table = build_kv_summary_table(key, value, layout, block_size=block_size, prototypes=summary_prototypes)
+    out = native.residual_sparse_attention(query, key, value, indices, nodes, table, scale=1.0 / math.sqrt(D))
     return out, None
 
 

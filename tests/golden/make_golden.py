@@ -220,10 +220,57 @@ def maxsim_cases(ref):
     return cases
 
 
+# name: (B, Hq, Hkv, T, D, dtype, seed, K, summary prototypes)
+RESIDUAL_CASES = {
+    "r_bf16": (1, 2, 1, 64 * 7 + 11, 64, torch.bfloat16, 31, 3, (1, 2, 4)),
+    "r_f32": (1, 2, 1, 64 * 5 + 5, 64, torch.float32, 32, 2, (4,)),
+}
+
+
+def _routes_with_gaps(B, G, qb, K, gen):
+    """int32 [B, 1, G, qb, K]: each row keeps its block and the one before (local window 1)
+    plus random earlier blocks, so the residual frontier is not empty."""
+    sel = torch.full((B, 1, G, qb, K), -1, dtype=torch.int32)
+    for b in range(B):
+        for g in range(G):
+            for q in range(qb):
+                must = {q, q - 1} - {-1}
+                rest = [int(x) for x in torch.randperm(max(q - 1, 0), generator=gen)]
+                row = sorted(must | set(rest[:max(0, K - len(must))]))
+                sel[b, 0, g, q, :len(row)] = torch.tensor(row, dtype=torch.int32)
+    return sel
+
+
+def residual_cases(ref):
+    """The reference's residual-summary attention (sparse/attention.py:83-274)."""
+    cases = {}
+    for name, (B, Hq, Hkv, T, D, dt, seed, K, protos) in RESIDUAL_CASES.items():
+        gen = torch.Generator().manual_seed(seed)
+        q = torch.randn((B, Hq, T, D), generator=gen).to(dt)
+        k = torch.randn((B, Hkv, T, D), generator=gen).to(dt)
+        v = torch.randn((B, Hkv, T, D), generator=gen).to(dt)
+        qb = (T + 63) // 64
+        sel = _routes_with_gaps(B, Hkv, qb, K, gen)
+        nodes = ref["summary_nodes"](sel)
+        cases[f"{name}_dtype"] = np.array([{torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}[dt]])
+        cases[f"{name}_q"], cases[f"{name}_k"], cases[f"{name}_v"] = _raw(q), _raw(k), _raw(v)
+        cases[f"{name}_selected"] = sel.numpy()
+        cases[f"{name}_nodes"] = nodes.numpy()
+        cases[f"{name}_protos"] = np.array(protos, dtype=np.int64)
+        for P in protos:
+            with torch.no_grad():
+                out, _ = ref["attention"](_Module(0), q, k, v, None, selected_blocks=sel, block_size=64,
+                                          residual_summaries=True, residual_summary_nodes=nodes,
+                                          summary_prototypes=P)
+            cases[f"{name}_out{P}"] = _raw(out)
+        print(f"{name}: qb={qb} residual width {nodes.shape[-1]}")
+    return cases
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("SPRUCE_REFERENCE", "/root/reference"))
-    ap.add_argument("--only", choices=["all", "summaries", "maxsim"], default="all")
+    ap.add_argument("--only", choices=["all", "summaries", "maxsim", "residual"], default="all")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     from teacher.chunked_extract import _group_avg_tokens, _proto_pool_seq
@@ -248,6 +295,9 @@ def main():
         return
     if args.only == "maxsim":
         np.savez_compressed(os.path.join(HERE, "maxsim.npz"), **maxsim_cases(ref))
+        return
+    if args.only == "residual":
+        np.savez_compressed(os.path.join(HERE, "residual.npz"), **residual_cases(ref))
         return
 
     for name, (shape, dtype, seed, rope, K, lw, sink, keep_blocks) in CASES.items():
@@ -280,6 +330,7 @@ def main():
     np.savez_compressed(os.path.join(HERE, "proto.npz"), **proto_cases(ref))
     np.savez_compressed(os.path.join(HERE, "summaries.npz"), **summary_cases(ref))
     np.savez_compressed(os.path.join(HERE, "maxsim.npz"), **maxsim_cases(ref))
+    np.savez_compressed(os.path.join(HERE, "residual.npz"), **residual_cases(ref))
     print("wrote", sorted(f for f in os.listdir(HERE) if f.endswith(".npz")))
 
 

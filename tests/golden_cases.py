@@ -144,3 +144,17 @@ def table_sha256(keys: torch.Tensor, values: torch.Tensor, counts: torch.Tensor)
     for a in (keys, values, counts):
         h.update(a.detach().cpu().contiguous().numpy().tobytes())
     return h.digest()
+
+
+RESIDUAL_CASE_NAMES = ("r_bf16", "r_f32")
+
+
+def load_residual_case(name: str):
+    """Inputs, routes, residual nodes and the reference's outputs per summary prototype count."""
+    z = load_npz("residual")
+    dt = DT[int(z[f"{name}_dtype"][0])]
+    q, k, v = (from_raw(z[f"{name}_{x}"], dt) for x in ("q", "k", "v"))
+    sel = torch.from_numpy(z[f"{name}_selected"])
+    nodes = torch.from_numpy(z[f"{name}_nodes"])
+    outs = {int(P): from_raw(z[f"{name}_out{int(P)}"], dt) for P in z[f"{name}_protos"]}
+    return q, k, v, sel, nodes, outs

@@ -115,7 +115,7 @@ def test_golden_fixtures_are_small():
     from golden_cases import HERE
 
     total = sum(os.path.getsize(os.path.join(HERE, f)) for f in os.listdir(HERE) if f.endswith(".npz"))
-    assert total < 6 * 2**20
+    assert total < 8 * 2**20
     assert np.load(os.path.join(HERE, "c0.npz"))["selected"].dtype == np.int32
 
 
@@ -165,3 +165,30 @@ def test_key_tree_and_traversal_match_reference():
         proj = [O.project(x, wk[0]) for x in levels]
         ids = O.traverse_to_leaf_ids(O.project(qf, wq[0]), proj, starts, beam=4)
         assert torch.equal(ids, torch.from_numpy(z[f"ms{n}_leaf_ids"])[0])
+
+
+@pytest.mark.parametrize("name", ["r_bf16", "r_f32"])
+def test_residual_attention_oracle_matches_reference(name):
+    # sparse/attention.py:83-274 with residual_summaries=True: the oracle's one
+    # softmax over selected blocks and residual summary keys, fed the oracle's
+    # summary table (bit-exact with build_kv_summary_table), reproduces the
+    # reference's outputs.
+    from golden_cases import load_residual_case
+    from spruce_research_b200.interfaces.residual_summaries import build_residual_tree_layout
+
+    q, k, v, sel, nodes, outs = load_residual_case(name)
+    T = q.shape[2]
+    lay = build_residual_tree_layout((T + 63) // 64)
+    assert nodes.shape[-1] > 0
+    for P, want in outs.items():
+        t = O.kv_summary_table(k, v, lay.starts, lay.ends, 64, P, None)
+        got = O.residual_sparse_attention(q, k, v, sel[:, 0], nodes[:, 0], t["keys"], t["values"], t["counts"],
+                                          t["log_counts"], out_dtype=torch.float32)
+        err = (got - want.float()).abs().max().item()
+        if q.dtype == torch.float32:
+            assert err < 2e-6, (P, err)
+        else:  # the reference rounds its fp32 result to bf16 once; so does the oracle's caller
+            assert (got.to(q.dtype).float() - want.float()).abs().max().item() <= 2 ** -7, (P, err)
+    # the summaries matter: without them the output differs
+    plain = O.sparse_attention(q, k, v, sel[:, 0], out_dtype=torch.float32)
+    assert (plain - outs[max(outs)].float()).abs().max().item() > 1e-2
