@@ -12,6 +12,7 @@ are all-gathered over NCCL; total work is fixed, so scaling is strong.
     python bench.py --sweep          # config 4: variable-length batch, densities 2..100%
     python bench.py --model          # config 3: whole-model prefill TTFT, dense vs SPRUCE flows
     python bench.py --tree-selector  # deployed selector (P=8 prototypes, key tree, beam 16) ms/layer
+    python bench.py --residual       # residual-summary attention (summary table + attention) ms/layer
 
 `value` is effective TFLOP/s of the selected tiles (algorithmic FLOPs of the
 step / device time of the step, max over ranks); `e2e` is the same metric
@@ -88,6 +89,8 @@ def parse_args():
     ap.add_argument("--model", action="store_true",
                     help="config 3 instead: whole Qwen2-7B-shaped model prefill TTFT, dense vs SPRUCE flows")
     ap.add_argument("--model-tokens", type=int, default=65536)
+    ap.add_argument("--residual", action="store_true",
+                    help="residual-summary attention at config 2 (summary table + attention, P = 1 and 4)")
     ap.add_argument("--tree-selector", action="store_true",
                     help="time the deployed tree selector (P=8, beam 16) beside the flat one at config 2's shape")
     return ap.parse_args()
@@ -740,6 +743,84 @@ def run_tree_selector(args):
     })
 
 
+def run_residual(args):
+    """Residual-summary attention at config 2 (sparse/attention.py:83-274 with residual_summaries=True):
+    the flat selector's routes at ``--density``, their maximal residual frontiers, and per step the
+    K/V summary table (built inside the reference's attention call) plus the attention over selected
+    blocks and summary keys.  Summary prototypes P = 1 and 4; plain block-sparse attention beside."""
+    import torch
+
+    from spruce_research_b200 import native
+    from spruce_research_b200.interfaces.residual_summaries import (build_residual_summary_nodes,
+                                                                    build_residual_tree_layout)
+    from spruce_research_b200.pipeline import SparsePrefillLayer
+    from spruce_research_b200.sparse.summaries import build_kv_summary_table
+    from spruce_research_b200.synthetic import make_gate_weights, make_layer_inputs
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    shape, K, entries, flops = workload(args)
+    qb, D, rep = shape.query_blocks, shape.head_dim, shape.q_heads // shape.kv_heads
+    q, k, v = make_layer_inputs(shape, torch.bfloat16, args.seed, device=dev)
+    wq, wk = make_gate_weights(1, D, D, args.seed + 1, device=dev)
+    sel = SparsePrefillLayer(wq[0], wk[0], K, local_window=0, sink_blocks=1).select(q, k)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    nodes = build_residual_summary_nodes(sel[:, None], validate_selected=False)[:, 0]
+    e1.record()
+    torch.cuda.synchronize()
+    frontier_ms = e0.elapsed_time(e1)
+    layout = build_residual_tree_layout(qb)
+    out = torch.empty((1, shape.tokens, shape.q_heads, D), device=dev, dtype=torch.bfloat16)
+
+    def timed(fn):
+        for _ in range(max(1, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / args.steps
+
+    plain_ms = timed(lambda: native.sparse_attention(q, k, v, sel, out=out))
+    rows = []
+    for P in (1, 4):
+        ws = {}
+
+        def step():
+            table = build_kv_summary_table(k, v, layout, block_size=64, prototypes=P)
+            native.residual_sparse_attention(q, k, v, sel, nodes, table, out=out, workspace=ws.get("w"))
+
+        table = build_kv_summary_table(k, v, layout, block_size=64, prototypes=P)
+        need = native._lib.load().spruce_residual_workspace_bytes(1, shape.kv_heads, shape.tokens, D,
+                                                                   nodes.shape[-1], P, 1)
+        ws["w"] = torch.empty(need, device=dev, dtype=torch.uint8)
+        step_ms = timed(step)
+        table_ms = timed(lambda: build_kv_summary_table(k, v, layout, block_size=64, prototypes=P))
+        attn_ms = timed(lambda: native.residual_sparse_attention(q, k, v, sel, nodes, table, out=out,
+                                                                 workspace=ws["w"]))
+        valid = table.counts[0][nodes.clamp(min=0).long()] > 0          # [G, qb, S, P]
+        summary_keys = int((valid & (nodes >= 0)[..., None]).sum())
+        sflops = 4.0 * D * rep * 64 * summary_keys  # every query token of the row's block scores every summary key
+        rows.append({"prototypes": P, "step_ms": step_ms, "table_ms": table_ms, "attention_ms": attn_ms,
+                     "summary_keys": summary_keys, "summary_tflop": sflops / 1e12,
+                     "effective_tflops": (flops + sflops) / (attn_ms * 1e-3) / 1e12,
+                     "workspace_gb": need / 1e9})
+        del ws
+    emit({
+        "metric": "residual-summary sparse prefill ms/layer at config 2 (summary table + attention)",
+        "value": rows[0]["step_ms"], "unit": "ms", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": rows[0]["step_ms"], "higher_is_better": False, "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1) Q/K/V, RoPE base 1e6, planted affinity",
+        "config": {**config_dict(args, shape, K, entries, 1), "residual_width": int(nodes.shape[-1]),
+                   "frontier_ms": frontier_ms},
+        "plain_attention_ms": plain_ms, "residual": rows,
+    })
+
+
 def main():
     args = parse_args()
     _claim_stdout()
@@ -751,6 +832,8 @@ def main():
         run_model(args)
     elif args.tree_selector:
         run_tree_selector(args)
+    elif args.residual:
+        run_residual(args)
     else:
         run_b200(args)
 

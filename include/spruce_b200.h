@@ -329,6 +329,18 @@ SPRUCE_API int spruce_ipc_export(const void *ptr, void *handle, int64_t *offset)
 SPRUCE_API int spruce_ipc_import(const void *handle, int64_t offset, void **ptr, void **base);
 SPRUCE_API int spruce_ipc_close(void *base);
 
+/* Maximal residual frontiers (interfaces/residual_summaries.py:122-220, build_residual_summary_nodes
+ * and residual_frontier_for_row): for each row of selected [rows, K] (int32, contiguous, -1 padded;
+ * row r is query block r % qb) the ID-sorted tree nodes that cover exactly the causal blocks the row
+ * leaves out, written to out [rows, S] with -1 padding.  The tree is ResidualTreeLayout's node table:
+ * node_starts / node_ends int64 [num_nodes] block ranges and node_parents int32 [num_nodes] (-1 for
+ * the root).  out may be NULL for a counting pass: row_counts [rows] (optional) receives each row's
+ * frontier size and *max_count (optional, zeroed by the caller) the largest. */
+SPRUCE_API int spruce_residual_frontier(const int32_t *selected, int64_t rows, int64_t K, int64_t qb,
+                                        const int64_t *node_starts, const int64_t *node_ends,
+                                        const int32_t *node_parents, int64_t num_nodes, int32_t *out, int64_t S,
+                                        int32_t *row_counts, int32_t *max_count, void *stream);
+
 /* Residual-summary attention (sparse/attention.py:83-274 with residual_summaries=True,
  * replacing its per-(query block, KV group) loop at :178-263): the block-sparse attention of
  * spruce_sparse_attention_fwd, where each row's softmax also covers the summary keys of its

@@ -56,6 +56,7 @@ SIGNATURES = {
     "spruce_kv_summary_workspace_bytes": ([_I64, _I64, _I64, _I64], _I64),
     "spruce_kv_summary_table": ([_P, _P, _P, _P, _P, _INT, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _I64,
                                  _P, _P, _P, _P, _P, _P, _P, _I64, _P], _INT),
+    "spruce_residual_frontier": ([_P, _I64, _I64, _I64, _P, _P, _P, _I64, _P, _I64, _P, _P, _P], _INT),
     "spruce_residual_workspace_bytes": ([_I64, _I64, _I64, _I64, _I64, _I64, _INT], _I64),
     "spruce_residual_sparse_attention_fwd": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _P, _P, _P, _P, _I64,
                                               _I64, _P, _P, _INT, _I64, _I64, _I64, _I64, _I64, _I64, _F, _P, _I64,

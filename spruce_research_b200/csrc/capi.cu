@@ -659,6 +659,25 @@ int spruce_residual_sparse_attention_fwd(const void* q, const int64_t q_strides[
                                                status, stream, &virt);
 }
 
+int spruce_residual_frontier(const int32_t* selected, int64_t rows, int64_t K, int64_t qb, const int64_t* node_starts,
+                             const int64_t* node_ends, const int32_t* node_parents, int64_t num_nodes, int32_t* out,
+                             int64_t S, int32_t* row_counts, int32_t* max_count, void* stream) {
+  if (rows < 0 || K < 0 || qb < 1 || num_nodes < 1 || S < 0)
+    return fail(SPRUCE_ERR_INVALID, "bad frontier shape (rows=%lld, K=%lld, qb=%lld, nodes=%lld, S=%lld)",
+                (long long)rows, (long long)K, (long long)qb, (long long)num_nodes, (long long)S);
+  if (rows % qb) return fail(SPRUCE_ERR_INVALID, "rows must be a multiple of the query-block count");
+  if (qb > 51200 || num_nodes > 2 * qb + 64 || K > 0x7fffffff)
+    return fail(SPRUCE_ERR_UNSUPPORTED, "frontier shape too large (qb=%lld)", (long long)qb);
+  if (rows == 0) return SPRUCE_OK;
+  if (selected == nullptr && K > 0) return fail(SPRUCE_ERR_INVALID, "selected is NULL");
+  if (node_starts == nullptr || node_ends == nullptr || node_parents == nullptr)
+    return fail(SPRUCE_ERR_INVALID, "tree layout arrays are NULL");
+  return cuda_status(spruce::launch_residual_frontier(selected, rows, (int)K, (int)qb, node_starts, node_ends,
+                                                      node_parents, (int)num_nodes, out, (int)S, row_counts,
+                                                      max_count, as_stream(stream)),
+                     "residual frontier launch");
+}
+
 int64_t spruce_kv_summary_workspace_bytes(int64_t B, int64_t Hkv, int64_t T, int64_t D) {
   if (B < 0 || Hkv < 0 || T < 0 || D < 0) return -1;
   return spruce::kv_summary_workspace_bytes(B, Hkv, T, D);

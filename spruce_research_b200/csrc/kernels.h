@@ -109,6 +109,11 @@ struct ResidualGatherArgs {
   int32_t* vcount;        // [B, Hkv, qb]
 };
 cudaError_t launch_residual_gather(const ResidualGatherArgs& a, int dtype, cudaStream_t stream);
+// Maximal residual frontier of each selected_blocks row (sel [rows, K] contiguous,
+// query block = row % qb); out [rows, S] ID-sorted, -1 padded (NULL: counts only).
+cudaError_t launch_residual_frontier(const int32_t* sel, int64_t rows, int K, int qb, const int64_t* starts,
+                                     const int64_t* ends, const int32_t* parents, int NN, int32_t* out, int S,
+                                     int32_t* row_counts, int32_t* max_count, cudaStream_t stream);
 
 // tcgen05 path (bf16 / fp16).  Returns cudaErrorInvalidValue for shapes it
 // does not cover (the C ABI checks them first).

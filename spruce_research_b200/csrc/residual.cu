@@ -80,7 +80,103 @@ __global__ void __launch_bounds__(kGatherThreads) residual_gather_kernel(const R
   if (threadIdx.x == 0) a.vcount[((int64_t)b * a.Hkv + g) * a.qb + i] = npad / 64;
 }
 
+// Maximal frontier of one selected_blocks row (interfaces/residual_summaries.py:122-155):
+// node n is taken when its block range lies inside the causal prefix [0, q] and
+// holds no selected block, and its parent's range does not (the reference's
+// depth-first visit stops exactly there: a parent that fails the test has an
+// ancestor chain that fails it too, since ranges only grow upwards).  Nodes are
+// scanned in ID order, so the row comes out ID-sorted like the reference's.
+// sel [rows, K] contiguous; a row's query block is row % qb.
+constexpr int kFrontierThreads = 256;
+
+__global__ void __launch_bounds__(kFrontierThreads)
+    residual_frontier_kernel(const int32_t* __restrict__ sel, int K, int qb, const int64_t* __restrict__ starts,
+                             const int64_t* __restrict__ ends, const int32_t* __restrict__ parents, int NN,
+                             int32_t* __restrict__ out, int S, int32_t* __restrict__ row_counts,
+                             int32_t* __restrict__ max_count) {
+  extern __shared__ int pre[];  // [qb + 1]: number of selected blocks below x
+  __shared__ int wsum[kFrontierThreads / 32];
+  const int64_t r = blockIdx.x;
+  const int q = (int)(r % qb);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int x = tid; x <= qb; x += kFrontierThreads) pre[x] = 0;
+  __syncthreads();
+  for (int c = tid; c < K; c += kFrontierThreads) {
+    const int id = sel[r * K + c];
+    if (id >= 0 && id < qb) pre[id + 1] = 1;  // duplicates mark once
+  }
+  __syncthreads();
+  // inclusive scan of pre[1..qb]: each thread one contiguous chunk, then a block scan of the chunk sums
+  const int per = (qb + kFrontierThreads - 1) / kFrontierThreads;
+  const int lo = 1 + tid * per, hi = min(qb + 1, lo + per);
+  int run = 0;
+  for (int x = lo; x < hi; ++x) run += pre[x];
+  int incl = run;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += y;
+  }
+  if (lane == 31) wsum[warp] = incl;
+  __syncthreads();
+  int base = 0;
+  for (int w = 0; w < warp; ++w) base += wsum[w];
+  int acc = base + incl - run;  // exclusive prefix of this thread's chunk
+  for (int x = lo; x < hi; ++x) {
+    acc += pre[x];
+    pre[x] = acc;
+  }
+  __syncthreads();
+  const int limit = q + 1;
+  auto empty_causal = [&](int n) {
+    const int s = (int)starts[n], e = (int)ends[n];
+    return e <= limit && pre[e] - pre[s] == 0;
+  };
+  int total = 0;
+  for (int n0 = 0; n0 < NN; n0 += kFrontierThreads) {  // uniform trip count
+    const int n = n0 + tid;
+    bool take = false;
+    if (n < NN && empty_causal(n)) {
+      const int par = parents[n];
+      take = par < 0 || !empty_causal(par);
+    }
+    const unsigned m = __ballot_sync(0xffffffffu, take);
+    __syncthreads();  // wsum reuse
+    if (lane == 0) wsum[warp] = __popc(m);
+    __syncthreads();
+    int before = total;
+    for (int w = 0; w < warp; ++w) before += wsum[w];
+    if (take && out != nullptr) {
+      const int pos = before + __popc(m & ((1u << lane) - 1u));
+      if (pos < S) out[r * S + pos] = n;
+    }
+    for (int w = 0; w < kFrontierThreads / 32; ++w) total += wsum[w];
+  }
+  if (out != nullptr)
+    for (int pos = total + tid; pos < S; pos += kFrontierThreads) out[r * S + pos] = -1;
+  if (tid == 0) {
+    if (row_counts != nullptr) row_counts[r] = total;
+    if (max_count != nullptr) atomicMax(max_count, total);
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_residual_frontier(const int32_t* sel, int64_t rows, int K, int qb, const int64_t* starts,
+                                     const int64_t* ends, const int32_t* parents, int NN, int32_t* out, int S,
+                                     int32_t* row_counts, int32_t* max_count, cudaStream_t stream) {
+  if (rows == 0) return cudaSuccess;
+  const size_t smem = sizeof(int) * ((size_t)qb + 1);
+  if (smem > 200 * 1024 || rows > 0x7fffffff) return cudaErrorInvalidValue;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(residual_frontier_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  residual_frontier_kernel<<<(unsigned)rows, kFrontierThreads, smem, stream>>>(sel, K, qb, starts, ends, parents, NN,
+                                                                              out, S, row_counts, max_count);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_residual_gather(const ResidualGatherArgs& a, int dtype, cudaStream_t stream) {
   if (a.B == 0 || a.Hkv == 0 || a.qb == 0) return cudaSuccess;

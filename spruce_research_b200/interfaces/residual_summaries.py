@@ -126,6 +126,24 @@ def residual_frontier_for_row(selected_block_ids: Sequence[int] | Iterable[int],
     return sorted(frontier)
 
 
+def layout_arrays(layout: ResidualTreeLayout, device) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """The node table on ``device``: starts / ends int64 and parents int32 (-1 for the root)."""
+    key = (layout.num_leaves, str(device))
+    hit = _LAYOUT_ARRAYS.get(key)
+    if hit is None:
+        top = len(layout.level_counts) - 1
+        parents = [layout.level_offsets[lv + 1] + idx // 2 if lv < top else -1
+                   for lv, idx in zip(layout.levels, layout.indices)]
+        hit = (torch.tensor(layout.starts, dtype=torch.int64, device=device),
+               torch.tensor(layout.ends, dtype=torch.int64, device=device),
+               torch.tensor(parents, dtype=torch.int32, device=device))
+        _LAYOUT_ARRAYS[key] = hit
+    return hit
+
+
+_LAYOUT_ARRAYS: dict = {}
+
+
 def _rows(t: torch.Tensor):
     a = t.detach().to(device="cpu")
     B, L, G, Q = a.shape[:4]
@@ -150,6 +168,11 @@ def build_residual_summary_nodes(selected_blocks: torch.Tensor, *, layout: Resid
         layout = build_residual_tree_layout(Q)
     elif layout.num_leaves != Q:
         raise ValueError(f"tree has {layout.num_leaves} leaves but selected_blocks has {Q} query blocks")
+    if selected_blocks.is_cuda:  # one GPU launch per pass instead of a Python walk per row
+        from .. import native
+
+        starts, ends, parents = layout_arrays(layout, selected_blocks.device)
+        return native.residual_frontier(selected_blocks, starts, ends, parents)
     frontiers = {}
     for (b, l, g, q), row in _rows(selected_blocks):
         frontiers[b, l, g, q] = residual_frontier_for_row([x for x in row if x != PAD_VALUE], q, layout)

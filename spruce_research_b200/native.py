@@ -272,6 +272,31 @@ def sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices:
     return out
 
 
+def residual_frontier(selected: torch.Tensor, starts: torch.Tensor, ends: torch.Tensor,
+                      parents: torch.Tensor) -> torch.Tensor:
+    """Maximal residual frontiers of selected_blocks rows [..., qb, K] -> int32 [..., qb, S], ID-sorted,
+    -1 padded, S the largest frontier (interfaces/residual_summaries.py:122-220).  starts / ends int64
+    and parents int32 [num_nodes] are the tree layout on the same device."""
+    _lib.require_cuda(selected, starts, ends, parents)
+    if selected.dtype != torch.int32 or selected.dim() < 2:
+        raise ValueError("selected_blocks must be int32 [..., qb, K]")
+    qb, K = selected.shape[-2:]
+    sel = selected.contiguous()
+    rows = math.prod(sel.shape[:-1])
+    L = _lib.load()
+    NN = starts.numel()
+    stream = _lib.stream_of(sel)
+    mx = torch.zeros(1, device=sel.device, dtype=torch.int32)
+    _lib.check(L.spruce_residual_frontier(sel.data_ptr(), rows, K, qb, starts.data_ptr(), ends.data_ptr(),
+                                          parents.data_ptr(), NN, None, 0, None, mx.data_ptr(), stream))
+    S = int(mx.item())
+    out = torch.empty((*sel.shape[:-1], S), device=sel.device, dtype=torch.int32)
+    if S:
+        _lib.check(L.spruce_residual_frontier(sel.data_ptr(), rows, K, qb, starts.data_ptr(), ends.data_ptr(),
+                                              parents.data_ptr(), NN, out.data_ptr(), S, None, None, stream))
+    return out
+
+
 def residual_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices: torch.Tensor,
                               nodes: torch.Tensor, table, scale: float | None = None,
                               out: torch.Tensor | None = None, status: torch.Tensor | None = None,

@@ -118,3 +118,30 @@ def test_residual_nodes_validate_routes_on_gpu():
     bad[0, 0, 0, 2] = torch.tensor([2, -1], dtype=torch.int32)
     with pytest.raises(AssertionError, match="Missing local-window"):
         build_residual_summary_nodes(bad.cuda())
+
+
+def test_frontier_kernel_matches_reference_golden():
+    # the c0 routes' frontiers as the reference's build_residual_summary_nodes made them
+    from golden_cases import load_npz
+
+    z = load_npz("summaries")
+    c0 = load_npz("c0")
+    selected = torch.from_numpy(c0["selected"])[:, None].contiguous()
+    nodes = build_residual_summary_nodes(selected.cuda(), validate_selected=False)
+    assert nodes.is_cuda and torch.equal(nodes.cpu(), torch.from_numpy(z["frontier_c0"]))
+
+
+@pytest.mark.parametrize("qb,K,seed", [(1, 1, 0), (2, 2, 1), (7, 3, 2), (100, 5, 3), (333, 9, 4), (2048, 24, 5)])
+def test_frontier_kernel_matches_host_walk(qb, K, seed):
+    # random causal routes (sorted, some rows short) against the reference-mirroring host walk
+    gen = torch.Generator().manual_seed(seed)
+    sel = torch.full((2, 1, 3, qb, K), -1, dtype=torch.int32)
+    for b in range(2):
+        for g in range(3):
+            for q in range(qb):
+                n = int(torch.randint(1, K + 1, (1,), generator=gen))
+                ids = sorted(set([q] + [int(x) for x in torch.randint(0, q + 1, (n - 1,), generator=gen)]))
+                sel[b, 0, g, q, :len(ids)] = torch.tensor(ids, dtype=torch.int32)
+    want = build_residual_summary_nodes(sel, validate_selected=False)
+    got = build_residual_summary_nodes(sel.cuda(), validate_selected=False)
+    assert got.shape == want.shape and torch.equal(got.cpu(), want)
