@@ -81,7 +81,7 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-chunks", type=int, default=16, help="query-block chunks of the streamed e2e step")
-    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target length of one CPU sample")
+    ap.add_argument("--cpu-seconds", type=float, default=24.0, help="target length of one CPU sample")
     ap.add_argument("--gather", choices=("fused", "nccl"), default="fused",
                     help="N>1 output all-gather: NVLink peer stores in the attention epilogue, or NCCL")
     ap.add_argument("--sweep", action="store_true",
