@@ -16,8 +16,7 @@
 // order into shared memory; then all 128 threads copy rows along D.
 #include <algorithm>
 
-#include "common.cuh"
-#include "kernels.h"
+#include "attn_common.cuh"
 
 namespace spruce {
 
@@ -25,7 +24,28 @@ namespace {
 
 constexpr int kGatherThreads = 128;
 
-template <typename T>
+template <typename T> struct Store4;
+template <> struct Store4<float> {
+  static __device__ __forceinline__ void put(float* dst, float4 v) { *reinterpret_cast<float4*>(dst) = v; }
+};
+template <> struct Store4<__nv_bfloat16> {
+  static __device__ __forceinline__ void put(__nv_bfloat16* dst, float4 v) {
+    uint2 u;
+    u.x = Pack2<__nv_bfloat16>::pack(v.x, v.y);
+    u.y = Pack2<__nv_bfloat16>::pack(v.z, v.w);
+    *reinterpret_cast<uint2*>(dst) = u;
+  }
+};
+template <> struct Store4<__half> {
+  static __device__ __forceinline__ void put(__half* dst, float4 v) {
+    uint2 u;
+    u.x = Pack2<__half>::pack(v.x, v.y);
+    u.y = Pack2<__half>::pack(v.z, v.w);
+    *reinterpret_cast<uint2*>(dst) = u;
+  }
+};
+
+template <typename T, int D>
 __global__ void __launch_bounds__(kGatherThreads) residual_gather_kernel(const ResidualGatherArgs a) {
   extern __shared__ int picks[];  // (slot * P + prototype) of the row's valid prototypes, in order
   __shared__ int npick;
@@ -49,35 +69,36 @@ __global__ void __launch_bounds__(kGatherThreads) residual_gather_kernel(const R
     if (lane == 0) npick = count;
   }
   __syncthreads();
+  // picks -> table row offsets (in units of D), in place
   const int n = min(npick, a.nvb * 64);
+  const int64_t bg = (int64_t)b * a.Hkv + g;
+  for (int r = threadIdx.x; r < n; r += kGatherThreads) {
+    const int pick = picks[r];
+    picks[r] = row[(pick / a.P) * a.ns[3]] * a.P + pick % a.P;  // node * P + prototype
+  }
+  __syncthreads();
   const int npad = (n + 63) / 64 * 64;
   const int64_t Tv = (int64_t)a.qb * a.nvb * 64;
-  const int64_t vrow0 = ((int64_t)b * a.Hkv + g) * Tv + (int64_t)i * a.nvb * 64;
-  T* vk = static_cast<T*>(a.vk) + vrow0 * a.D;
-  T* vv = static_cast<T*>(a.vv) + vrow0 * a.D;
-  for (int e = threadIdx.x; e < npad * a.D; e += kGatherThreads) {
-    const int r = e / a.D, d = e % a.D;
-    float kx = 0.0f, vx = 0.0f;
+  const int64_t vrow0 = bg * Tv + (int64_t)i * a.nvb * 64;
+  T* vk = static_cast<T*>(a.vk) + vrow0 * D;
+  T* vv = static_cast<T*>(a.vv) + vrow0 * D;
+  const float* keys = a.keys + bg * a.NN * a.P * D;
+  const float* values = a.values + bg * a.NN * a.P * D;
+  constexpr int V4 = D / 4;  // float4 chunks per row
+  for (int e = threadIdx.x; e < npad * V4; e += kGatherThreads) {
+    const int r = e / V4, c = e % V4;  // V4 is a power of two: shifts
+    float4 kx = make_float4(0.0f, 0.0f, 0.0f, 0.0f), vx = kx;
     if (r < n) {
-      const int pick = picks[r];
-      const int node = row[(pick / a.P) * a.ns[3]];
-      const int64_t src = ((((int64_t)b * a.Hkv + g) * a.NN + node) * a.P + pick % a.P) * a.D + d;
-      kx = a.keys[src];
-      vx = a.values[src];
+      const int64_t src = (int64_t)picks[r] * D + 4 * c;
+      kx = __ldg(reinterpret_cast<const float4*>(keys + src));
+      vx = __ldg(reinterpret_cast<const float4*>(values + src));
     }
-    vk[e] = Elem<T>::from_f(kx);
-    vv[e] = Elem<T>::from_f(vx);
+    Store4<T>::put(vk + (int64_t)r * D + 4 * c, kx);
+    Store4<T>::put(vv + (int64_t)r * D + 4 * c, vx);
   }
-  for (int r = threadIdx.x; r < npad; r += kGatherThreads) {
-    float bias = -INFINITY;
-    if (r < n) {
-      const int pick = picks[r];
-      const int node = row[(pick / a.P) * a.ns[3]];
-      bias = a.log_counts[((int64_t)b * a.NN + node) * a.P + pick % a.P];
-    }
-    a.vbias[vrow0 + r] = bias;
-  }
-  if (threadIdx.x == 0) a.vcount[((int64_t)b * a.Hkv + g) * a.qb + i] = npad / 64;
+  for (int r = threadIdx.x; r < npad; r += kGatherThreads)
+    a.vbias[vrow0 + r] = r < n ? a.log_counts[(int64_t)b * a.NN * a.P + picks[r]] : -INFINITY;
+  if (threadIdx.x == 0) a.vcount[bg * a.qb + i] = npad / 64;
 }
 
 // Maximal frontier of one selected_blocks row (interfaces/residual_summaries.py:122-155):
@@ -178,37 +199,33 @@ cudaError_t launch_residual_frontier(const int32_t* sel, int64_t rows, int K, in
   return cudaGetLastError();
 }
 
+template <typename T, int D>
+static cudaError_t gather_typed(const ResidualGatherArgs& a, size_t smem, cudaStream_t stream) {
+  cudaError_t e = cudaFuncSetAttribute(residual_gather_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid((unsigned)a.qb, (unsigned)a.Hkv, (unsigned)a.B);
+  residual_gather_kernel<T, D><<<grid, kGatherThreads, smem, stream>>>(a);
+  return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t gather_d(const ResidualGatherArgs& a, size_t smem, cudaStream_t stream) {
+  if (a.D == 128) return gather_typed<T, 128>(a, smem, stream);
+  if (a.D == 64) return gather_typed<T, 64>(a, smem, stream);
+  return cudaErrorInvalidValue;
+}
+
 cudaError_t launch_residual_gather(const ResidualGatherArgs& a, int dtype, cudaStream_t stream) {
   if (a.B == 0 || a.Hkv == 0 || a.qb == 0) return cudaSuccess;
   const size_t smem = sizeof(int) * (size_t)std::max(1, a.S * a.P);
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
-  dim3 grid((unsigned)a.qb, (unsigned)a.Hkv, (unsigned)a.B);
   switch (dtype) {
-    case SPRUCE_DTYPE_F32: {
-      cudaError_t e = cudaFuncSetAttribute(residual_gather_kernel<float>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e != cudaSuccess) return e;
-      residual_gather_kernel<float><<<grid, kGatherThreads, smem, stream>>>(a);
-      break;
-    }
-    case SPRUCE_DTYPE_BF16: {
-      cudaError_t e = cudaFuncSetAttribute(residual_gather_kernel<__nv_bfloat16>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e != cudaSuccess) return e;
-      residual_gather_kernel<__nv_bfloat16><<<grid, kGatherThreads, smem, stream>>>(a);
-      break;
-    }
-    case SPRUCE_DTYPE_F16: {
-      cudaError_t e = cudaFuncSetAttribute(residual_gather_kernel<__half>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e != cudaSuccess) return e;
-      residual_gather_kernel<__half><<<grid, kGatherThreads, smem, stream>>>(a);
-      break;
-    }
-    default:
-      return cudaErrorInvalidValue;
+    case SPRUCE_DTYPE_F32: return gather_d<float>(a, smem, stream);
+    case SPRUCE_DTYPE_BF16: return gather_d<__nv_bfloat16>(a, smem, stream);
+    case SPRUCE_DTYPE_F16: return gather_d<__half>(a, smem, stream);
+    default: return cudaErrorInvalidValue;
   }
-  return cudaGetLastError();
 }
 
 }  // namespace spruce
