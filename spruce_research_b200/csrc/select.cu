@@ -21,26 +21,27 @@ namespace spruce {
 // ------------------------------------------------------------------ projection
 
 // Row n of the launch is row (n / nrows) * qb + row0 + n % nrows of x (and of out).
-// kProjRows rows per 128-thread CTA: the rows are staged in shared memory,
-// thread p keeps one accumulator per row and reads 16 weights at a time.
+// ROWS rows per 128-thread CTA (4, or 16 when there are many rows so that W
+// is read from L2 fewer times): the rows are staged in shared memory, thread
+// p keeps one accumulator per row and reads 16 weights at a time.
 // Each output is one fma chain over d = 0..D-1 in order.
 constexpr int kProjRows = 4;
 
-template <typename T>
+template <typename T, int ROWS>
 __global__ void __launch_bounds__(128) project_kernel(const T* __restrict__ x, int64_t N, int D,
                                                       const float* __restrict__ W, int P, float* __restrict__ out,
                                                       int qb, int row0, int nrows) {
-  extern __shared__ float xs[];  // [kProjRows][D]
-  const int64_t n0 = (int64_t)blockIdx.x * kProjRows;
-  const int rows = (int)(N - n0 < kProjRows ? N - n0 : kProjRows);
+  extern __shared__ float xs[];  // [ROWS][D]
+  const int64_t n0 = (int64_t)blockIdx.x * ROWS;
+  const int rows = (int)(N - n0 < ROWS ? N - n0 : ROWS);
   auto map_row = [&](int64_t n) { return (n / nrows) * qb + row0 + n % nrows; };
   for (int e = threadIdx.x; e < rows * D; e += blockDim.x) xs[e] = Elem<T>::to_f(x[map_row(n0 + e / D) * D + e % D]);
-  for (int e = rows * D + threadIdx.x; e < kProjRows * D; e += blockDim.x) xs[e] = 0.0f;
+  for (int e = rows * D + threadIdx.x; e < ROWS * D; e += blockDim.x) xs[e] = 0.0f;
   __syncthreads();
   for (int p = threadIdx.x; p < P; p += blockDim.x) {
-    float acc[kProjRows];
+    float acc[ROWS];
 #pragma unroll
-    for (int r = 0; r < kProjRows; ++r) acc[r] = 0.0f;
+    for (int r = 0; r < ROWS; ++r) acc[r] = 0.0f;
     int d = 0;
     for (; d + 16 <= D; d += 16) {  // 16 weight loads in flight, then the chains in d order
       float w[16];
@@ -49,12 +50,12 @@ __global__ void __launch_bounds__(128) project_kernel(const T* __restrict__ x, i
 #pragma unroll
       for (int u = 0; u < 16; ++u)
 #pragma unroll
-        for (int r = 0; r < kProjRows; ++r) acc[r] = __fmaf_rn(xs[r * D + d + u], w[u], acc[r]);
+        for (int r = 0; r < ROWS; ++r) acc[r] = __fmaf_rn(xs[r * D + d + u], w[u], acc[r]);
     }
     for (; d < D; ++d) {
       const float w = __ldg(W + (int64_t)d * P + p);
 #pragma unroll
-      for (int r = 0; r < kProjRows; ++r) acc[r] = __fmaf_rn(xs[r * D + d], w, acc[r]);
+      for (int r = 0; r < ROWS; ++r) acc[r] = __fmaf_rn(xs[r * D + d], w, acc[r]);
     }
     for (int r = 0; r < rows; ++r) out[map_row(n0 + r) * P + p] = acc[r];
   }
@@ -609,8 +610,14 @@ cudaError_t launch_project_rows(const void* x, int64_t groups, int qb, int row0,
                                                                               out, qb, row0, nrows);
     return cudaGetLastError();
   }
+  if (N >= (int64_t)148 * 16 * 8) {  // many rows: 16 per CTA, so W is read from L2 a quarter as often
+    const size_t smem = sizeof(float) * 16 * D;
+    project_kernel<T, 16><<<(unsigned)((N + 15) / 16), 128, smem, stream>>>(static_cast<const T*>(x), N, D, W, P,
+                                                                           out, qb, row0, nrows);
+    return cudaGetLastError();
+  }
   const size_t smem = sizeof(float) * kProjRows * D;
-  project_kernel<T><<<(unsigned)((N + kProjRows - 1) / kProjRows), 128, smem, stream>>>(
+  project_kernel<T, kProjRows><<<(unsigned)((N + kProjRows - 1) / kProjRows), 128, smem, stream>>>(
       static_cast<const T*>(x), N, D, W, P, out, qb, row0, nrows);
   return cudaGetLastError();
 }
@@ -827,8 +834,11 @@ __global__ void __launch_bounds__(32) maxsim_lane_kernel(const float* __restrict
   constexpr int STAGE = 32 * KS + P * kMsChunk;
   extern __shared__ __align__(16) float lsm[];
   const int lane = threadIdx.x;
-  const int64_t rq = blockIdx.x;
-  const int64_t r = rq / nq;
+  // consecutive CTAs take different r, so the few nodes of a narrow tree level
+  // are not all read by every resident CTA at once
+  const int64_t R = gridDim.x / nq;
+  const int64_t r = blockIdx.x % R;
+  const int64_t rq = r * nq + blockIdx.x / R;
   const float* qrow = qp + rq * P * pdim;
   const int nch = pdim / kMsChunk;
   for (int c0 = 0; c0 < ncols; c0 += 32) {
