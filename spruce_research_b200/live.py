@@ -119,14 +119,14 @@ class LiveSelector:
             return int(self.k_selected)
         return max(k_for_density(query_blocks, self.density), self.local_window + 1 + self.sink_blocks)
 
+    @torch.no_grad()
     def _layer_gate(self, layer_idx: int) -> FlatGate:
+        """A one-layer FlatGate holding this layer's projections (the tree routines index layer 0)."""
         gate = self._layer_gates.get(layer_idx)
         if gate is None:
-            gate = FlatGate.__new__(FlatGate)
-            torch.nn.Module.__init__(gate)
-            gate.proj_dim = self._wq.shape[2]
-            gate.Wq = torch.nn.Parameter(self._wq[layer_idx:layer_idx + 1], requires_grad=False)
-            gate.Wk = torch.nn.Parameter(self._wk[layer_idx:layer_idx + 1], requires_grad=False)
+            gate = FlatGate(1, self._wq.shape[1], self._wq.shape[2]).to(self._wq.device).eval()
+            gate.Wq.copy_(self._wq[layer_idx:layer_idx + 1])
+            gate.Wk.copy_(self._wk[layer_idx:layer_idx + 1])
             self._layer_gates[layer_idx] = gate
         return gate
 
