@@ -297,9 +297,9 @@ SPRUCE_API int spruce_sparse_attention_fwd_rows(const void *q, const int64_t q_s
 
 /*
  * spruce_sparse_attention_fwd_rows with the output all-gather fused into the
- * kernel's epilogue, for layers whose query heads are split across GPUs (the
- * NCCL all-gather of per-head outputs of SURVEY multi-GPU plan, done as
- * NVLink peer stores while the attention runs).  Each output row is written to
+ * kernel's epilogue, for layers whose query heads are split across GPUs (in
+ * place of an NCCL all-gather of the per-head outputs: NVLink peer stores made
+ * while the attention runs).  Each output row is written to
  * `out` and, at the same element offset, to every `peer_outs[i]` (n_peers <=
  * 7): device pointers of identically laid out tensors on the other GPUs,
  * mapped into this process (CUDA IPC) with peer access.  Plain stores; no

@@ -269,9 +269,12 @@ def residual_cases(ref):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("SPRUCE_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("SPRUCE_REFERENCE"),
+                    help="path of the reference checkout (or set SPRUCE_REFERENCE)")
     ap.add_argument("--only", choices=["all", "summaries", "maxsim", "residual"], default="all")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference (or SPRUCE_REFERENCE): the reference checkout to run")
     sys.path.insert(0, args.reference)
     from teacher.chunked_extract import _group_avg_tokens, _proto_pool_seq
     from selector.gate import FlatGate
