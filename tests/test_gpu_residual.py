@@ -120,3 +120,59 @@ def test_no_residual_nodes_is_plain_sparse_attention():
     table = build_kv_summary_table(k, v, build_residual_tree_layout(qb), block_size=64, prototypes=1)
     got = native.residual_sparse_attention(q, k, v, sel.cuda(), nodes[:, 0].cuda(), table)
     assert torch.equal(got, native.sparse_attention(q, k, v, sel.cuda()))
+
+
+def _prefix_mean(v, Hq):
+    """Uniform causal attention: out[b, t, h] = mean(v[b, g(h), :t+1]) in fp64, [B, T, Hq, D]."""
+    c = torch.cumsum(v.double(), dim=2) / torch.arange(1, v.shape[2] + 1, device=v.device,
+                                                        dtype=torch.float64)[None, None, :, None]
+    return c.repeat_interleave(Hq // v.shape[1], dim=1).transpose(1, 2)
+
+
+@pytest.mark.parametrize("P", [1, 2, 4])
+def test_identical_keys_give_dense_attention(P):
+    # tests/test_summary_pooling.py:100-131 of the reference: with every key equal, a summary
+    # prototype weighted by its count stands in exactly for its tokens, so the residual-summary
+    # output is dense causal attention -- here uniform over the causal prefix
+    gen = torch.Generator().manual_seed(90 + P)
+    B, Hq, Hkv, T, D = 1, 8, 2, 64 * 37 + 21, 128
+    q = torch.randn((B, Hq, T, D), generator=gen).to(torch.bfloat16).cuda()
+    k = torch.randn((B, Hkv, 1, D), generator=gen).to(torch.bfloat16).expand(B, Hkv, T, D).contiguous().cuda()
+    v = torch.randn((B, Hkv, T, D), generator=gen).to(torch.bfloat16).cuda()
+    sel = _routes(B, Hkv, (T + 63) // 64, 5, 91)
+    out, _ = sparse_prefill_attention_forward(_Layer(), q, k, v, None, selected_blocks=sel.cuda(), block_size=64,
+                                              residual_summaries=True,
+                                              residual_summary_nodes=build_residual_summary_nodes(sel.cuda()),
+                                              summary_prototypes=P)
+    _close(out, _prefix_mean(v, Hq), torch.bfloat16)
+
+
+def test_identical_keys_at_config2_shape():
+    # the same property at 131072 tokens, 28/4 heads, d=128, routes of the flat selector at 10%
+    from spruce_research_b200.pipeline import SparsePrefillLayer
+    from spruce_research_b200.synthetic import k_for_density, make_gate_weights
+
+    gen = torch.Generator().manual_seed(95)
+    B, Hq, Hkv, T, D = 1, 28, 4, 131072, 128
+    q = torch.randn((B, T, Hq, D), generator=gen).to(torch.bfloat16).cuda().transpose(1, 2)
+    k = torch.randn((B, Hkv, 1, D), generator=gen).to(torch.bfloat16).cuda().expand(B, Hkv, T, D).contiguous()
+    v = torch.randn((B, T, Hkv, D), generator=gen).to(torch.bfloat16).cuda().transpose(1, 2)
+    wq, wk = make_gate_weights(1, D, D, 96, device="cuda")
+    sel = SparsePrefillLayer(wq[0], wk[0], k_for_density(T // 64, 0.10), 0, 1).select(q, k)
+    nodes = build_residual_summary_nodes(sel[:, None], validate_selected=False)[:, 0]
+    assert nodes.shape[-1] > 10  # equal scores: the selector keeps the lowest ids, leaving one long gap per row
+    table = build_kv_summary_table(k, v, build_residual_tree_layout(T // 64), block_size=64, prototypes=4)
+    out = native.residual_sparse_attention(q, k, v, sel, nodes, table)
+    want = _prefix_mean(v, Hq)
+    err = (out.double() - want).abs()
+    assert err.max().item() < 2e-2 and err.mean().item() < 2e-3, (err.max().item(), err.mean().item())
+
+
+def test_summaries_disabled_is_identical():
+    # tests/test_summary_pooling.py:134-160 of the reference
+    q, k, v, sel, nodes, _ = load_residual_case("r_bf16")
+    args = dict(selected_blocks=sel.cuda(), block_size=64)
+    base, _ = sparse_prefill_attention_forward(_Layer(), q.cuda(), k.cuda(), v.cuda(), None, **args)
+    off, _ = sparse_prefill_attention_forward(_Layer(), q.cuda(), k.cuda(), v.cuda(), None, residual_summaries=False,
+                                              residual_summary_nodes=nodes.cuda(), summary_prototypes=4, **args)
+    assert torch.equal(base, off)
