@@ -26,6 +26,37 @@ class KeyTreeLevel:
     ends: torch.Tensor
 
 
+def _level_ranges(kb: int, radix: int) -> list[tuple[list[int], list[int]]]:
+    """Leaf-block ranges of every level: parent j spans children j*radix .. (j+1)*radix - 1 (selector/tree.py:116-145)."""
+    starts, ends = list(range(kb)), list(range(1, kb + 1))
+    out = [(starts, ends)]
+    while len(starts) > 1:
+        n = len(starts)
+        m = (n + radix - 1) // radix
+        starts = [starts[j * radix] for j in range(m)]
+        ends = [ends[min((j + 1) * radix, n) - 1] for j in range(m)]
+        out.append((starts, ends))
+    return out
+
+
+_RANGE_CACHE: dict = {}
+
+
+def _level_range_tensors(kb: int, radix: int, device) -> list[tuple[torch.Tensor, torch.Tensor]]:
+    """The ranges as int64 tensors on ``device``, built once per (kb, radix, device) and shared (read-only)."""
+    key = (kb, radix, str(device))
+    hit = _RANGE_CACHE.get(key)
+    if hit is None:
+        ranges = _level_ranges(kb, radix)
+        flat = torch.tensor([x for st, en in ranges for x in st + en], dtype=torch.int64).to(device)
+        hit, off = [], 0
+        for st, en in ranges:
+            hit.append((flat[off:off + len(st)], flat[off + len(st):off + 2 * len(st)]))
+            off += 2 * len(st)
+        _RANGE_CACHE[key] = hit
+    return hit
+
+
 def build_key_tree(k_feat: torch.Tensor, radix: int = 2) -> list[KeyTreeLevel]:
     """Levels leaf-first from leaf key features ``[L, G, kb, P, d]``; odd tails are smaller parents."""
     if radix < 2:
@@ -33,20 +64,14 @@ def build_key_tree(k_feat: torch.Tensor, radix: int = 2) -> list[KeyTreeLevel]:
     if k_feat.dim() != 5:
         raise ValueError(f"k_feat must be [L,G,kb,P,d], got {tuple(k_feat.shape)}")
     L, G, kb, P, d = k_feat.shape
-    dev = k_feat.device
-    starts = torch.arange(kb, device=dev, dtype=torch.long)
-    levels = [KeyTreeLevel(0, k_feat, starts, starts + 1)]
+    ranges = _level_range_tensors(kb, radix, k_feat.device)  # pure functions of kb and radix
+    levels = [KeyTreeLevel(0, k_feat, *ranges[0])]
     current = k_feat.reshape(L * G, kb, P, d)
     level = 0
     while current.shape[1] > 1:
         level += 1
-        n = current.shape[1]
-        prev = levels[-1]
         current = native.tree_merge(current, radix)
-        parents = torch.arange(current.shape[1], device=dev)
-        starts = prev.starts[parents * radix]
-        ends = prev.ends[((parents + 1) * radix - 1).clamp_max(n - 1)]
-        levels.append(KeyTreeLevel(level, current.view(L, G, -1, P, d), starts, ends))
+        levels.append(KeyTreeLevel(level, current.view(L, G, -1, P, d), *ranges[level]))
     return levels
 
 

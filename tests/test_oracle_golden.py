@@ -192,3 +192,19 @@ def test_residual_attention_oracle_matches_reference(name):
     # the summaries matter: without them the output differs
     plain = O.sparse_attention(q, k, v, sel[:, 0], out_dtype=torch.float32)
     assert (plain - outs[max(outs)].float()).abs().max().item() > 1e-2
+
+
+def test_key_tree_level_ranges_match_reference():
+    # selector/tree.py's level ranges, computed once on the host, against the reference's stored levels
+    from spruce_research_b200.selector.tree import _level_ranges
+
+    z = load_npz("maxsim")
+    for n in range(2):
+        kb = z[f"ms{n}_tree0"].shape[2]
+        ranges = _level_ranges(kb, 2)
+        level = 0
+        while f"ms{n}_tree{level}_range" in z:
+            want = z[f"ms{n}_tree{level}_range"]
+            assert ranges[level] == (want[0].tolist(), want[1].tolist()), (n, level)
+            level += 1
+        assert level == len(ranges)
