@@ -166,6 +166,45 @@ __global__ void tree_topk_kernel(const float* __restrict__ scores, const uint8_t
   }
 }
 
+// The same selection for rows of at most 32 candidates (every level of a beam-16,
+// radix-2 traversal): each lane holds one candidate as a 64-bit key -- the
+// order-preserving image of its score (-0 folded into +0) above 31 - position --
+// and the warp sorts the keys descending with a bitonic network.  Keys are
+// distinct, and their order is the float order of the scores with ties to the
+// lower position, so the first k lanes hold exactly what tree_topk_kernel picks
+// (for scores that are not NaN).
+__device__ __forceinline__ uint32_t float_order_key(float f) {
+  const uint32_t u = __float_as_uint(f + 0.0f);  // -0 -> +0
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__global__ void tree_topk32_kernel(const float* __restrict__ scores, const uint8_t* __restrict__ valid,
+                                   const int64_t* __restrict__ cand, int C, int k, int64_t rows,
+                                   int64_t* __restrict__ out) {
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;  // warp-uniform
+  uint64_t key = 0;         // below every real candidate
+  if (lane < C) {
+    const float x = valid[row * C + lane] ? scores[row * C + lane] : -3.402823466e38f;
+    key = ((uint64_t)float_order_key(x) << 32) | (uint32_t)(31 - lane);
+  }
+#pragma unroll
+  for (int size = 2; size <= 32; size <<= 1) {
+    const bool desc = (lane & size) == 0;  // the last merge (size 32) is descending for every lane
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      const uint64_t other = __shfl_xor_sync(0xffffffffu, key, stride);
+      const bool keep_max = ((lane & stride) == 0) == desc;
+      key = keep_max ? (key > other ? key : other) : (key < other ? key : other);
+    }
+  }
+  if (lane < k) {
+    const int pos = 31 - (int)(key & 0xffffffffu);
+    out[row * k + lane] = valid[row * C + pos] ? cand[row * C + pos] : -1;
+  }
+}
+
 }  // namespace
 
 template <typename T>
@@ -198,6 +237,10 @@ cudaError_t launch_tree_topk(const float* scores, const uint8_t* valid, const in
                              int k, int64_t* out, cudaStream_t stream) {
   if (rows == 0 || k == 0) return cudaSuccess;
   if (C > kMaxCand || k > C) return cudaErrorInvalidValue;
+  if (C <= 32) {
+    tree_topk32_kernel<<<(unsigned)((rows + 3) / 4), 128, 0, stream>>>(scores, valid, cand, C, k, rows, out);
+    return cudaGetLastError();
+  }
   tree_topk_kernel<<<(unsigned)((rows + 3) / 4), 128, 0, stream>>>(scores, valid, cand, C, k, rows, out);
   return cudaGetLastError();
 }

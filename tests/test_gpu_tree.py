@@ -98,3 +98,22 @@ def test_maxsim_shapes_match_oracle(P, p, nk):
     shifted = flat[1:].view(qp.shape)
     shifted.copy_(qp.cuda())
     assert torch.equal(native.gate_maxsim(shifted, kp.cuda(), ids.cuda()).cpu(), O.maxsim(qp, kp, ids))
+
+
+@pytest.mark.parametrize("C", [1, 5, 17, 32, 33, 64])
+def test_tree_topk_matches_stable_sort(C):
+    # best k per row by score (invalid slots scored as the fp32 minimum), ties to the lower
+    # position: a stable descending sort; C <= 32 takes the bitonic kernel, wider rows the scan
+    gen = torch.Generator().manual_seed(70 + C)
+    rows = 300
+    scores = torch.randn((1, rows, C), generator=gen)
+    scores[..., ::3] = torch.round(scores[..., ::3])           # ties
+    scores[0, :7, 0] = -0.0
+    valid = torch.rand((1, rows, C), generator=gen) > 0.25
+    cand = torch.randint(0, 10_000, (1, rows, C), generator=gen)
+    for k in sorted({1, max(1, C // 2), C}):
+        got = native.tree_topk(scores.cuda(), valid.to(torch.uint8).cuda(), cand.cuda(), k).cpu()
+        x = torch.where(valid, scores, torch.full_like(scores, -3.402823466e38))
+        order = torch.sort(x, dim=-1, descending=True, stable=True).indices[..., :k]
+        want = torch.where(torch.gather(valid, -1, order), torch.gather(cand, -1, order), torch.full_like(order, -1))
+        assert torch.equal(got, want), (C, k)
