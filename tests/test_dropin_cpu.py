@@ -111,3 +111,27 @@ def test_block_mask_launcher_checks_and_index_conversion():
     q = torch.zeros(1, 2, 130, 64)
     with pytest.raises(RuntimeError, match="CUDA"):
         block_sparse_triton(q, q, q, mask, 0.1)
+
+
+def test_residual_summary_keyword_errors_follow_reference():
+    # sparse/attention.py:113-141 of the reference: prototype and mode checks, then the residual
+    # checks in order (missing nodes, learned mode without / with a checkpoint, node validation),
+    # all before any CUDA requirement
+    query = torch.randn(1, 2, 4, 4)
+    key = value = torch.randn(1, 2, 4, 4)
+    sel = _selected(groups=2)
+    args = dict(selected_blocks=sel, block_size=2)
+    with pytest.raises(ValueError, match="summary_prototypes must be one of"):
+        sparse_prefill_attention_forward(_Module(), query, key, value, None, summary_prototypes=3, **args)
+    with pytest.raises(ValueError, match="summary_mode must be one of"):
+        sparse_prefill_attention_forward(_Module(), query, key, value, None, summary_mode="max", **args)
+    with pytest.raises(ValueError, match="requires residual_summary_nodes"):
+        sparse_prefill_attention_forward(_Module(), query, key, value, None, residual_summaries=True, **args)
+    nodes = torch.full((1, 1, 2, 2, 1), -1, dtype=torch.int32)
+    with pytest.raises(ValueError, match="requires summary_checkpoint"):
+        sparse_prefill_attention_forward(_Module(), query, key, value, None, residual_summaries=True,
+                                         residual_summary_nodes=nodes, summary_mode="learned", **args)
+    with pytest.raises(NotImplementedError, match="learned compressor"):
+        sparse_prefill_attention_forward(_Module(), query, key, value, None, residual_summaries=True,
+                                         residual_summary_nodes=nodes, summary_mode="learned",
+                                         summary_checkpoint="ckpt.pt", **args)
