@@ -6,7 +6,6 @@ tests/test_export_selected_blocks.py and tests/test_validator.py of the
 reference, rewritten for 64-token blocks and checked against the oracle or the
 reference's golden outputs.
 """
-import math
 
 import numpy as np
 import pytest
