@@ -223,7 +223,9 @@ def cpu_sample(shape, K, q, k, v, wq, wk, target_s: float, rows: int | None = No
     top-k, packing) plus attention of the last M query blocks (each with K
     selected blocks); M is calibrated so one sample takes ~target_s seconds.
     Returned TFLOP/s = attention FLOPs of the M rows / (attention time + the
-    selector time prorated to M/qb of the rows).
+    selector time prorated to M/qb of the rows).  The third value holds the
+    oracle's group-0 selection and the fp32 output rows of the sample, which
+    the GPU arm compares with its own step.
     """
     import torch
 
@@ -239,10 +241,11 @@ def cpu_sample(shape, K, q, k, v, wq, wk, target_s: float, rows: int | None = No
     t0 = time.perf_counter()
     sel = O.select_blocks(q0, k0, wq, wk, K, 0, 1)["selected"]
     t_sel = time.perf_counter() - t0
+    last = {}
 
     def attn_rows(m):
         t = time.perf_counter()
-        O.sparse_attention(q0, k0, v0, sel, out_dtype=torch.float32, q_blocks=(qb - m, qb))
+        last["out"] = O.sparse_attention(q0, k0, v0, sel, out_dtype=torch.float32, q_blocks=(qb - m, qb))
         return time.perf_counter() - t
 
     m = rows
@@ -251,13 +254,38 @@ def cpu_sample(shape, K, q, k, v, wq, wk, target_s: float, rows: int | None = No
         m = int(max(1, min(qb, round(4 * max(target_s, 0.5) / max(t4, 1e-3)))))
     best = attn_rows(m) + t_sel * m / qb
     rows_flops = 4.0 * shape.head_dim * rep * m * ((K - 1) * 4096 + 64 * 65 / 2)
+    checked = {"selected_g0": sel[:, 0], "out_rows": last["out"][:, (qb - m) * 64:], "blocks": (qb - m, qb)}
     return {
         "value": rows_flops / best / 1e12, "unit": "TFLOP/s", "cores": O.num_threads(), "kind": "port",
         "seconds": best,
         "sample": (f"oracle C port (OpenMP, {O.num_threads()} threads): KV group 0 selector "
                    f"({t_sel:.2f} s, prorated {m}/{qb}) + attention of the last {m} query blocks x {rep} heads, "
                    f"K={K}; fp32 math on bf16 inputs"),
-    }, m
+    }, m, checked
+
+
+def headline_fixture(args, shape, K):
+    """The reference's outputs for this exact workload (tests/golden/c2.npz), or None.
+
+    They exist for BASELINE config 2 with the default inputs: 131072 tokens, 10%
+    density, seed 0 (gate seed 1).
+    """
+    path = os.path.join(ROOT, "tests", "golden", "c2.npz")
+    if not os.path.exists(path):
+        return None
+    import numpy as np
+
+    z = np.load(path)
+    shp = [int(x) for x in z["shape"]]
+    if (shp != [shape.batch, shape.q_heads, shape.kv_heads, shape.tokens, shape.head_dim]
+            or int(z["policy"][0]) != K or int(z["seed"][0]) != args.seed or int(z["wseed"][0]) != args.seed + 1):
+        return None
+    return z
+
+
+def attention_error(got, want) -> dict:
+    err = (got.float().cpu() - want.float().cpu()).abs()
+    return {"max_abs": err.max().item(), "mean_abs": err.mean().item()}
 
 
 # ----------------------------------------------------------------- GPU arm
@@ -287,8 +315,11 @@ def run_b200(args):
 
     shape, K, entries, flops = workload(args)
     qb = shape.query_blocks
-    q, k, v = make_layer_inputs(shape, torch.bfloat16, args.seed, device=dev)
-    wq, wk = make_gate_weights(1, shape.head_dim, shape.head_dim, args.seed + 1, device=dev)
+    # Made on the CPU (seeded torch.Generator), as the golden fixtures' inputs are, then moved to
+    # HBM in the [B, T, H, D] storage the reference's callers hand over.
+    q_host, k_host, v_host = make_layer_inputs(shape, torch.bfloat16, args.seed)
+    q, k, v = (t.transpose(1, 2).to(dev).transpose(1, 2) for t in (q_host, k_host, v_host))
+    wq, wk = (w.to(dev) for w in make_gate_weights(1, shape.head_dim, shape.head_dim, args.seed + 1))
     layer = SparsePrefillLayer(wq[0], wk[0], K, local_window=0, sink_blocks=1)
     # the fused gather takes unequal chunks, so its half-group split balances selected tiles
     shard = plan(world, rank, shape.kv_heads, qb, k_selected=K if args.gather == "fused" else None)
@@ -406,10 +437,40 @@ def run_b200(args):
                                                 "attend and its output shard (bytes summed over ranks)"))}
         del dq, dk, dv
 
+    # ---- parity of this very workload (untimed): the reference's outputs, then the oracle's
+    full = step(q_shard, k_shard, v_shard)
+    torch.cuda.synchronize()
+    parity = {}
+    fixture = headline_fixture(args, shape, K)
+    if fixture is not None:
+        import numpy as np
+
+        cs = np.array([t.double().sum().item() for t in (q_host, k_host, v_host)])
+        if np.allclose(cs, fixture["checksum"], rtol=1e-12, atol=1e-6):
+            want = torch.from_numpy(fixture["selected"].astype(np.int32))[:, g0:g1, i0:i1].to(dev)
+            counts = torch.tensor([(sel_buf[:, :, i0:i1] == want).all(-1).sum().item(), want[..., 0].numel()],
+                                  dtype=torch.float64, device=dev)
+            if world > 1:
+                dist.all_reduce(counts)
+            blocks = [int(b) for b in fixture["out_blocks"]]
+            rows = torch.cat([torch.arange(b * 64, min((b + 1) * 64, T)) for b in blocks]).to(dev)
+            ref_out = torch.from_numpy(fixture["out"]).view(torch.bfloat16)
+            parity["reference"] = {"rows_equal": int(counts[0].item()), "rows_total": int(counts[1].item()),
+                                   "sampled_query_blocks": blocks,
+                                   "attn": attention_error(full[:, rows], ref_out),
+                                   "source": "tests/golden/c2.npz: the reference's own selector and "
+                                             "sparse_prefill_attention_forward on these inputs"}
+        else:
+            parity["reference"] = {"skipped": "this host regenerated other inputs than the fixture's"}
+
     # ---- CPU baseline (rank 0, single GPU only)
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
-        cpu, _ = cpu_sample(shape, K, q, k, v, wq[0], wk[0], args.cpu_seconds)
+        cpu, _, checked = cpu_sample(shape, K, q_host, k_host, v_host, wq[0], wk[0], args.cpu_seconds)
+        c0, c1 = checked["blocks"]
+        parity["oracle"] = {"rows_equal": int((sel_buf[:, 0].cpu() == checked["selected_g0"]).all(-1).sum()),
+                            "rows_total": qb, "kv_group": 0, "query_blocks": [c0, c1],
+                            "attn": attention_error(full[:, c0 * 64:c1 * 64, 0:rep], checked["out_rows"])}
 
     peak, peak_src = measured_peak()
     r_flops = shard_flops(shape, K, shard)
@@ -437,6 +498,7 @@ def run_b200(args):
                      "flops_per_launch": r_flops, "traffic": profiled_traffic(shape.tokens)},
         "gpu_launches": SparsePrefillLayer.LAUNCHES_PER_CALL * args.steps,
         "clocks": clocks.summary(),
+        "parity": parity,
     }
     if e2e is not None:
         result["e2e"] = e2e
@@ -463,14 +525,14 @@ def run_reference(args):
     if int(os.environ.get("RANK", "0")) != 0:
         return
     shape, K, entries, flops = workload(args)
-    dev = "cuda" if torch.cuda.is_available() else "cpu"
-    q, k, v = make_layer_inputs(shape, torch.bfloat16, args.seed, device=dev)
-    wq, wk = make_gate_weights(1, shape.head_dim, shape.head_dim, args.seed + 1, device=dev)
+    # the GPU arm's inputs: made on the CPU from the same seeds
+    q, k, v = make_layer_inputs(shape, torch.bfloat16, args.seed)
+    wq, wk = make_gate_weights(1, shape.head_dim, shape.head_dim, args.seed + 1)
     # Size the sample once (about cpu_seconds of CPU work), then time it per step.
-    info, m = cpu_sample(shape, K, q, k, v, wq[0], wk[0], target_s=min(args.cpu_seconds, 8.0))
+    info, m, _ = cpu_sample(shape, K, q, k, v, wq[0], wk[0], target_s=min(args.cpu_seconds, 8.0))
     steps = []
     for s in range(args.warmup + args.steps):
-        r, _ = cpu_sample(shape, K, q, k, v, wq[0], wk[0], 0.0, rows=m)
+        r, _, _ = cpu_sample(shape, K, q, k, v, wq[0], wk[0], 0.0, rows=m)
         if s >= args.warmup:
             steps.append(r["value"])
             info = r

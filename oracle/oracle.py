@@ -240,6 +240,28 @@ def sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices:
     return out.to(out_dtype or q.dtype)
 
 
+def sparse_attention_blocks(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices: torch.Tensor,
+                            blocks, scale: float | None = None, block: int = 64) -> torch.Tensor:
+    """The rows of the listed query blocks only: [B, rows, Hq, D] fp32, rows in list order.
+
+    Same arithmetic as sparse_attention; the inputs are converted to fp32 once.
+    """
+    B, Hq, T, D = q.shape
+    Hkv = k.shape[1]
+    if scale is None:
+        scale = D ** -0.5
+    qf = q.detach().float().cpu().contiguous()
+    kf = k.detach().float().cpu().contiguous()
+    vf = v.detach().float().cpu().contiguous()
+    idx = indices.detach().cpu().to(torch.int32).contiguous()
+    out = torch.zeros((B, T, Hq, D), dtype=torch.float32)
+    for i in blocks:
+        lib().oracle_sparse_attention_rows(_ptr(qf), _ptr(kf), _ptr(vf), _ptr(idx), B, Hq, Hkv, T, D,
+                                           idx.shape[-1], block, float(scale), int(i), int(i) + 1, _ptr(out))
+    rows = torch.cat([torch.arange(i * block, min((i + 1) * block, T)) for i in blocks])
+    return out[:, rows]
+
+
 def residual_sparse_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, indices: torch.Tensor,
                               nodes: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, counts: torch.Tensor,
                               log_counts: torch.Tensor, scale: float | None = None, block: int = 64,

@@ -46,6 +46,17 @@ CASES = {
 }
 
 
+# The headline configurations in full.  name: (shape, dtype, input seed, gate-weight seed, rope,
+# K (None = 10% charged density), local_window, sink, sampled query blocks of the stored attention)
+BIG_CASES = {
+    # 32768 tokens, 10% density (K = 27).
+    "c1_full": (LayerShape(1, 28, 4, 32768, 128), torch.bfloat16, 21, 22, 1e6, None, 0, 1, (0, 1, 256, 510, 511)),
+    # 131072 tokens, 10% density (K = 106), with bench.py's default inputs
+    # (input seed 0, gate seed 1), so the bench can check its own step against these outputs.
+    "c2": (LayerShape(1, 28, 4, 131072, 128), torch.bfloat16, 0, 1, 1e6, None, 0, 1, (0, 1, 1024, 2046, 2047)),
+}
+
+
 def _raw(t: torch.Tensor) -> np.ndarray:
     t = t.detach().cpu().contiguous()
     if t.dtype in (torch.bfloat16, torch.float16):
@@ -92,6 +103,76 @@ def reference_pipeline(ref, q, k, v, wq, wk, K, local_window, sink):
         "pooled_q": pooled_q[:, :, :, 0], "pooled_k": pooled_k[:, :, :, 0],
         "scores": torch.stack(scores), "selected": selected_blocks[:, 0], "out": out,
     }
+
+
+def big_case(ref, name):
+    """One headline configuration in full, through the reference's own functions.
+
+    The gate runs one KV group at a time (the reference's scores are elementwise per
+    (group, query block, key block), so this changes no bit and bounds host memory).
+    Stored: the whole selected_blocks (int16: ids < 2^15), the score gap at each row's
+    selection boundary (the W-th minus the (W+1)-th largest candidate score, +inf when
+    the row has no (W+1)-th candidate), SHA-256 digests of the pooled features, and the
+    attention output of a few sampled query blocks.
+    """
+    import hashlib
+    import time
+
+    shape, dtype, seed, wseed, rope, K, lw, sink, keep = BIG_CASES[name]
+    t0 = time.time()
+    q, k, v = make_layer_inputs(shape, dtype, seed, rope_theta=rope)
+    wq, wk = make_gate_weights(1, shape.head_dim, shape.head_dim, wseed)
+    qb = shape.query_blocks
+    if K is None:
+        K = k_for_density(qb, 0.10)
+    B, G = shape.batch, shape.kv_heads
+    pooled_q = ref["proto_pool"](ref["group_avg"](q, G), 64, 1)        # [B, G, qb, 1, d]
+    pooled_k = ref["proto_pool"](k, 64, 1)
+    gate = ref["FlatGate"](1, shape.head_dim, shape.head_dim).eval()
+    with torch.no_grad():
+        gate.Wq.copy_(wq)
+        gate.Wk.copy_(wk)
+    qi = torch.arange(qb)[:, None]
+    kj = torch.arange(qb)[None, :]
+    forced_or_future = (kj > qi) | (kj >= qi - lw) | ((kj < sink) & (kj < qi - lw))
+    width = min(K - (lw + 1) - sink, qb)
+    selected = torch.empty((B, G, qb, K), dtype=torch.int32)
+    gap = torch.full((B, G, qb), float("inf"), dtype=torch.float32)
+    floor = torch.finfo(torch.float32).min
+    for b in range(B):
+        for g in range(G):
+            with torch.no_grad():
+                s = gate(pooled_q[b, g:g + 1].float().unsqueeze(0), pooled_k[b, g:g + 1].float().unsqueeze(0))
+            masked = s.masked_fill(forced_or_future[None, None], floor)    # [1, 1, qb, kb]
+            ids = masked.topk(width, dim=-1).indices
+            sel = ref["pack"](ids, k_selected=K, local_window=lw, key_blocks=qb, sink_blocks=sink)
+            ref["validate"](sel, local_window=lw)
+            selected[b, g] = sel[0, 0, 0]
+            top = masked[0, 0].topk(min(width + 1, qb), dim=-1).values     # [qb, width + 1]
+            if top.shape[-1] > width:
+                real = top[:, width] > floor
+                gap[b, g, real] = (top[real, width - 1] - top[real, width])
+            del s, masked
+    t_sel = time.time() - t0
+    out, _ = ref["attention"](_Module(), q, k, v, None, selected_blocks=selected[:, None].contiguous(),
+                              block_size=64, validate_selected_blocks_input=False)
+    rows = torch.cat([torch.arange(i * 64, min((i + 1) * 64, shape.tokens)) for i in keep])
+    digest = {}
+    for key, t in (("pooled_q", pooled_q), ("pooled_k", pooled_k)):
+        digest[key] = np.frombuffer(hashlib.sha256(_raw(t).tobytes()).digest(), dtype=np.uint8)
+    np.savez_compressed(
+        os.path.join(HERE, f"{name}.npz"),
+        shape=np.array([shape.batch, shape.q_heads, shape.kv_heads, shape.tokens, shape.head_dim]),
+        dtype=np.array([{torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}[dtype]]),
+        seed=np.array([seed]), wseed=np.array([wseed]), rope=np.array([rope if rope is not None else 0.0]),
+        policy=np.array([K, lw, sink]),
+        checksum=np.array([q.double().sum().item(), k.double().sum().item(), v.double().sum().item()]),
+        pooled_q_sha256=digest["pooled_q"], pooled_k_sha256=digest["pooled_k"],
+        selected=selected.to(torch.int16).numpy(), gap=gap.numpy(),
+        out=_raw(out[:, rows]), out_blocks=np.array(keep, dtype=np.int64),
+    )
+    print(f"{name}: K={K} selector {t_sel:.1f} s, total {time.time() - t0:.1f} s; "
+          f"smallest boundary gap {gap.min().item():.3e}, rows with gap < 1e-6: {(gap < 1e-6).sum().item()}")
 
 
 def packing_cases(ref):
@@ -271,7 +352,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("SPRUCE_REFERENCE"),
                     help="path of the reference checkout (or set SPRUCE_REFERENCE)")
-    ap.add_argument("--only", choices=["all", "summaries", "maxsim", "residual"], default="all")
+    ap.add_argument("--only", choices=["all", "summaries", "maxsim", "residual", "c1_full", "c2"], default="all")
     args = ap.parse_args()
     if not args.reference:
         ap.error("give --reference (or SPRUCE_REFERENCE): the reference checkout to run")
@@ -301,6 +382,9 @@ def main():
         return
     if args.only == "residual":
         np.savez_compressed(os.path.join(HERE, "residual.npz"), **residual_cases(ref))
+        return
+    if args.only in BIG_CASES:
+        big_case(ref, args.only)
         return
 
     for name, (shape, dtype, seed, rope, K, lw, sink, keep_blocks) in CASES.items():
@@ -334,6 +418,8 @@ def main():
     np.savez_compressed(os.path.join(HERE, "summaries.npz"), **summary_cases(ref))
     np.savez_compressed(os.path.join(HERE, "maxsim.npz"), **maxsim_cases(ref))
     np.savez_compressed(os.path.join(HERE, "residual.npz"), **residual_cases(ref))
+    for name in BIG_CASES:
+        big_case(ref, name)
     print("wrote", sorted(f for f in os.listdir(HERE) if f.endswith(".npz")))
 
 

@@ -158,3 +158,82 @@ def load_residual_case(name: str):
     nodes = torch.from_numpy(z[f"{name}_nodes"])
     outs = {int(P): from_raw(z[f"{name}_out{int(P)}"], dt) for P in z[f"{name}_protos"]}
     return q, k, v, sel, nodes, outs
+
+
+BIG_CASE_NAMES = ("c1_full", "c2")
+
+
+@dataclass
+class BigCase:
+    """A headline configuration in full (c1_full: BASELINE config 1, c2: config 2).
+
+    Holds the reference's whole selected_blocks, the score gap at each row's
+    selection boundary, digests of its pooled features and the attention output
+    of a few sampled query blocks (tests/golden/make_golden.py, big_case).
+    """
+
+    name: str
+    shape: LayerShape
+    dtype: torch.dtype
+    seed: int
+    wseed: int
+    rope: float | None
+    K: int
+    local_window: int
+    sink: int
+    z: dict
+
+    def inputs(self):
+        """(q, k, v, wq, wk) on the CPU: [B, H, T, D] views of token-major storage, [d, p] weights."""
+        q, k, v = make_layer_inputs(self.shape, self.dtype, self.seed, rope_theta=self.rope)
+        wq, wk = make_gate_weights(1, self.shape.head_dim, self.shape.head_dim, self.wseed)
+        return q, k, v, wq[0], wk[0]
+
+    def same_inputs(self, q, k, v) -> bool:
+        """True when these are the inputs the reference saw (see GoldenCase.matches_fixture)."""
+        cs = np.array([q.double().sum().item(), k.double().sum().item(), v.double().sum().item()])
+        return bool(np.allclose(cs, self.z["checksum"], rtol=1e-12, atol=1e-6))
+
+    @property
+    def selected(self) -> torch.Tensor:
+        """int32 [B, Hkv, qb, K]."""
+        return torch.from_numpy(self.z["selected"].astype(np.int32))
+
+    @property
+    def gap(self) -> torch.Tensor:
+        return torch.from_numpy(self.z["gap"])
+
+    @property
+    def out(self) -> torch.Tensor:
+        """The reference's attention output at out_rows(): [B, rows, Hq, D] in the input dtype."""
+        return from_raw(self.z["out"], self.dtype)
+
+    @property
+    def out_blocks(self) -> list:
+        return [int(i) for i in self.z["out_blocks"]]
+
+    def out_rows(self) -> torch.Tensor:
+        T = self.shape.tokens
+        return torch.cat([torch.arange(b * 64, min((b + 1) * 64, T)) for b in self.out_blocks])
+
+    def digest(self, key: str) -> bytes:
+        return bytes(self.z[f"{key}_sha256"].tolist())
+
+
+def load_big_case(name: str) -> BigCase:
+    z = load_npz(name)
+    B, Hq, Hkv, T, D = (int(x) for x in z["shape"])
+    K, lw, sink = (int(x) for x in z["policy"])
+    rope = float(z["rope"][0]) or None
+    return BigCase(name, LayerShape(B, Hq, Hkv, T, D), DT[int(z["dtype"][0])], int(z["seed"][0]),
+                   int(z["wseed"][0]), rope, K, lw, sink, z)
+
+
+def raw_sha256(t: torch.Tensor) -> bytes:
+    """SHA-256 of a tensor's bytes in its own dtype (bf16/fp16 as their 16-bit patterns)."""
+    import hashlib
+
+    t = t.detach().cpu().contiguous()
+    if t.dtype in (torch.bfloat16, torch.float16):
+        t = t.view(torch.int16)
+    return hashlib.sha256(t.numpy().tobytes()).digest()

@@ -208,3 +208,47 @@ def test_key_tree_level_ranges_match_reference():
             assert ranges[level] == (want[0].tolist(), want[1].tolist()), (n, level)
             level += 1
         assert level == len(ranges)
+
+
+# ---------------------------------------------------------------- the headline configurations in full
+_BIG = {}
+
+
+def _big(name):
+    """(case, inputs, oracle selector result), computed once per module."""
+    from golden_cases import load_big_case
+
+    if name not in _BIG:
+        case = load_big_case(name)
+        q, k, v, wq, wk = case.inputs()
+        assert case.same_inputs(q, k, v), "synthetic generator drifted"
+        _BIG[name] = (case, (q, k, v, wq, wk), O.select_blocks(q, k, wq, wk, case.K, case.local_window, case.sink))
+    return _BIG[name]
+
+
+@pytest.mark.parametrize("name", ["c1_full", "c2"])
+def test_headline_pooled_features_bit_exact(name):
+    from golden_cases import raw_sha256
+
+    case, _, r = _big(name)
+    assert raw_sha256(r["pooled_q"]) == case.digest("pooled_q")
+    assert raw_sha256(r["pooled_k"]) == case.digest("pooled_k")
+
+
+@pytest.mark.parametrize("name", ["c1_full", "c2"])
+def test_headline_selected_blocks_bit_exact(name):
+    """Every row of the reference's selection at config 1 (32K, K=27) and config 2 (128K, K=106)."""
+    case, _, r = _big(name)
+    differ = (r["selected"] != case.selected).any(-1)
+    assert not differ.any(), (f"{int(differ.sum())} of {differ.numel()} rows differ; their boundary score gaps: "
+                              f"{case.gap[differ][:8].tolist()}")
+
+
+@pytest.mark.parametrize("name", ["c1_full", "c2"])
+def test_headline_attention_rows_match_reference(name):
+    case, (q, k, v, _, _), _ = _big(name)
+    out = O.sparse_attention_blocks(q, k, v, case.selected, case.out_blocks)
+    err = (out - case.out.float()).abs()
+    # the reference's output is rounded to bf16: within one ulp of |x| <= 8
+    assert err.max().item() < 1.6e-2
+    assert err.mean().item() < 1e-3
