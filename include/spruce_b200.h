@@ -187,7 +187,8 @@ SPRUCE_API int spruce_gate_select_rows(const float *qp, const float *kp, int64_t
                                        const int64_t out_strides[3], int64_t q_block_begin, int64_t q_block_end,
                                        void *stream);
 
-/* Bytes of workspace spruce_select_blocks needs for this shape. */
+/* Bytes of workspace spruce_select_blocks needs for this shape; -1 for an
+ * invalid shape or a size that would not fit in int64. */
 SPRUCE_API int64_t spruce_select_workspace_bytes(int64_t B, int64_t Hkv, int64_t T, int64_t D, int64_t P, int dtype);
 
 /*
@@ -228,7 +229,11 @@ SPRUCE_API int spruce_select_blocks_rows(const void *q, const int64_t q_strides[
  * call on a device looks up the array's device address (cudaGetSymbolAddress)
  * with that device current; make that first call before any stream capture.
  * All calls share the one array: calls that overlap on the GPU (different
- * streams, or other host threads) race on it; serialise them.
+ * streams, or other host threads) race on it; serialise them.  The looked-up
+ * address is kept per device for the life of the process, so do not use this
+ * entry point across a cudaDeviceReset (which tears down the module that holds
+ * the array).  Shapes whose scratch size does not fit in int64 are rejected
+ * with SPRUCE_ERR_INVALID before any device work.
  */
 SPRUCE_API int spruce_select_blocks_noalloc(const void *q, const int64_t q_strides[4], const void *k,
                                             const int64_t k_strides[4], int dtype, int64_t B, int64_t Hq,
@@ -328,6 +333,16 @@ SPRUCE_API int spruce_sparse_attention_fwd_scatter(const void *q, const int64_t 
 SPRUCE_API int spruce_ipc_export(const void *ptr, void *handle, int64_t *offset);
 SPRUCE_API int spruce_ipc_import(const void *handle, int64_t offset, void **ptr, void **base);
 SPRUCE_API int spruce_ipc_close(void *base);
+
+/*
+ * Self-check hook with no counterpart in the reference.  The attention
+ * softmax computes part of its exponentials with a polynomial on the FMA pipe
+ * (Cody-Waite reduction, a degree-3 polynomial fitted for this library) and the
+ * rest with the MUFU ex2.approx instruction.  This evaluates both over x[0..n)
+ * (device pointers, fp32) into poly_out / mufu_out, so tests can check the
+ * polynomial's error bound and its agreement with MUFU after bf16 rounding.
+ */
+SPRUCE_API int spruce_exp2_selfcheck(const float *x, int64_t n, float *poly_out, float *mufu_out, void *stream);
 
 /* Maximal residual frontiers (interfaces/residual_summaries.py:122-220, build_residual_summary_nodes
  * and residual_frontier_for_row): for each row of selected [rows, K] (int32, contiguous, -1 padded;

@@ -277,10 +277,18 @@ int spruce_gate_select(const float* qp, const float* kp, int64_t B, int64_t G, i
 }
 
 int64_t spruce_select_workspace_bytes(int64_t B, int64_t Hkv, int64_t T, int64_t D, int64_t P, int dtype) {
-  const int64_t qb = (T + SPRUCE_BLOCK - 1) / SPRUCE_BLOCK;
-  const int64_t rows = B * Hkv * qb;
+  // -1 for a shape the selector rejects anyway, or whose size would not fit in int64:
+  // a wrapped product must never pass a workspace-size check.
+  if (!valid_dtype(dtype) || B < 0 || Hkv < 1 || T < 0 || D < 1 || D > 256 || P < 1 || P > 1024) return -1;
+  const int64_t qb = T / SPRUCE_BLOCK + (T % SPRUCE_BLOCK != 0);
+  int64_t rows = 0, feat = 0, proj = 0;
+  if (__builtin_mul_overflow(B, Hkv, &rows) || __builtin_mul_overflow(rows, qb, &rows)) return -1;
+  if (qb > INT32_MAX || rows > INT32_MAX) return -1;  // the kernels index query blocks and rows with int
+  if (__builtin_mul_overflow(rows, D * elem_size(dtype), &feat) || __builtin_mul_overflow(rows, P * 4, &proj))
+    return -1;
+  if (feat > INT64_MAX / 4 - 256 || proj > INT64_MAX / 4 - 256) return -1;
   auto up = [](int64_t x) { return (x + 255) / 256 * 256; };
-  return 2 * up(rows * D * elem_size(dtype)) + 2 * up(rows * P * 4);
+  return 2 * up(feat) + 2 * up(proj);
 }
 
 int spruce_select_blocks(const void* q, const int64_t q_strides[4], const void* k, const int64_t k_strides[4],
@@ -302,6 +310,9 @@ int spruce_select_blocks_rows(const void* q, const int64_t q_strides[4], const v
   int rc = check_select_policy(K, local_window, sink_blocks);
   if (rc) return rc;
   const int64_t need = spruce_select_workspace_bytes(B, Hkv, T, D, P, dtype);
+  if (need < 0)
+    return fail(SPRUCE_ERR_INVALID, "bad selector shape (B=%lld, Hkv=%lld, T=%lld, D=%lld, P=%lld, dtype %d)",
+                (long long)B, (long long)Hkv, (long long)T, (long long)D, (long long)P, dtype);
   if (workspace_bytes < need)
     return fail(SPRUCE_ERR_WORKSPACE, "workspace of %lld bytes, need %lld", (long long)workspace_bytes,
                 (long long)need);
@@ -406,6 +417,9 @@ int spruce_select_blocks_noalloc(const void* q, const int64_t q_strides[4], cons
                                  int32_t* out, const int64_t out_strides[3], void* stream) {
   if (!valid_dtype(dtype)) return fail(SPRUCE_ERR_INVALID, "unsupported dtype code %d", dtype);
   const int64_t need = spruce_select_workspace_bytes(B, Hkv, T, D, P, dtype);
+  if (need < 0)
+    return fail(SPRUCE_ERR_INVALID, "bad selector shape (B=%lld, Hkv=%lld, T=%lld, D=%lld, P=%lld)", (long long)B,
+                (long long)Hkv, (long long)T, (long long)D, (long long)P);
   if (need > kNoAllocScratchBytes)
     return fail(SPRUCE_ERR_UNSUPPORTED,
                 "spruce_select_blocks_noalloc: this shape needs %lld bytes of scratch, more than the %lld-byte "
@@ -566,6 +580,13 @@ static int spruce_sparse_attention_fwd_rows_impl(const void* q, const int64_t q_
     return fail(SPRUCE_ERR_UNSUPPORTED, "row width %lld exceeds %d", (long long)kw_all,
                 spruce::attn_sm100_max_kw((int)D));
   return cuda_status(spruce::launch_attn_sm100(a, dtype, as_stream(stream)), "tcgen05 attention launch");
+}
+
+int spruce_exp2_selfcheck(const float* x, int64_t n, float* poly_out, float* mufu_out, void* stream) {
+  if (n < 0) return fail(SPRUCE_ERR_INVALID, "n must be >= 0");
+  if (n > 0 && (x == nullptr || poly_out == nullptr || mufu_out == nullptr))
+    return fail(SPRUCE_ERR_INVALID, "null pointer");
+  return cuda_status(spruce::launch_exp2_probe(x, poly_out, mufu_out, n, as_stream(stream)), "exp2 probe launch");
 }
 
 int spruce_sparse_attention_fwd(const void* q, const int64_t q_strides[4], const void* k, const int64_t k_strides[4],

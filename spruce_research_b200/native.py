@@ -159,7 +159,10 @@ def _check_rows_out(out: torch.Tensor, B: int, G: int, qb: int, K: int) -> None:
 
 def select_workspace_bytes(q: torch.Tensor, k: torch.Tensor, proj_dim: int) -> int:
     B, _, T, d = q.shape
-    return int(_lib.load().spruce_select_workspace_bytes(B, k.shape[1], T, d, proj_dim, _dt(q)))
+    need = int(_lib.load().spruce_select_workspace_bytes(B, k.shape[1], T, d, proj_dim, _dt(q)))
+    if need < 0:
+        raise ValueError(f"bad selector shape: q {tuple(q.shape)}, k {tuple(k.shape)}, proj_dim {proj_dim}")
+    return need
 
 
 def select_blocks(q: torch.Tensor, k: torch.Tensor, Wq: torch.Tensor, Wk: torch.Tensor, k_selected: int,

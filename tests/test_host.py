@@ -50,6 +50,22 @@ def test_policy_errors_are_value_errors_before_any_device_work():
         _lib.check(rc)
 
 
+def test_selector_sizes_that_would_overflow_are_rejected_before_any_device_work():
+    """A shape whose scratch size does not fit in int64 (or whose rows overflow the kernels'
+    int indices) gets size -1 and an ERR_INVALID from both selector entry points, so a
+    wrapped product can never pass the no-allocation entry point's 16 MiB check."""
+    L = _lib.load()
+    huge_t = 1 << 62
+    assert L.spruce_select_workspace_bytes(1, 4, huge_t, 128, 128, 1) == -1
+    assert L.spruce_select_workspace_bytes(1 << 40, 1 << 20, 1 << 20, 128, 128, 1) == -1
+    assert L.spruce_select_workspace_bytes(1, 4, 131072, 128, 128, 1) == 12582912   # config 2: 12 MiB
+    s4 = (ctypes.c_int64 * 4)(1, 1, 1, 1)
+    args = (None, s4, None, s4, 1, 1, 28, 4, huge_t, 128, None, None, 128, 106, 0, 1, None, _lib.int64s(1, 1, 1))
+    assert L.spruce_select_blocks_noalloc(*args, None) == _lib.ERR_INVALID
+    assert "bad selector shape" in L.spruce_last_error().decode()
+    assert L.spruce_select_blocks_rows(*args, 0, 1, None, 1 << 30, None) == _lib.ERR_INVALID
+
+
 def test_cpu_tensors_are_rejected_without_fallback():
     x = torch.zeros(1, 2, 64, 64, dtype=torch.bfloat16)
     idx = torch.zeros(1, 1, 1, 1, dtype=torch.int32)

@@ -20,12 +20,15 @@ from spruce_research_b200.synthetic import LayerShape, k_for_density, make_gate_
 pytestmark = pytest.mark.gpu
 
 
-def _noalloc(q, k, wq, wk, K, local_window, sink):
+def _noalloc(q, k, wq, wk, K, local_window, sink, out=None):
+    """One call of the C entry point; `out` (int32 [B, Hkv, qb, K]) and fp32 contiguous
+    weights are the caller's buffers, so with them given this makes no allocation at all."""
     L = _lib.load()
     B, Hq, T, d = q.shape
     Hkv = k.shape[1]
     qb = (T + 63) // 64
-    out = torch.full((B, Hkv, qb, K), -7, device=q.device, dtype=torch.int32)
+    if out is None:
+        out = torch.full((B, Hkv, qb, K), -7, device=q.device, dtype=torch.int32)
     wq = wq.float().contiguous()
     wk = wk.float().contiguous()
     rc = L.spruce_select_blocks_noalloc(
@@ -64,3 +67,26 @@ def test_noalloc_rejects_shapes_beyond_its_static_scratch():
                                         _lib.int64s(1, 1, 1), _lib.stream_of(dummy))
     assert rc == _lib.ERR_UNSUPPORTED
     assert "static buffer" in L.spruce_last_error().decode()
+
+
+def test_noalloc_allocates_nothing_and_serves_config2():
+    """At BASELINE config 2's shape (131072 tokens, 12 MiB of scratch, the largest case the
+    16 MiB array is documented to hold): same rows as the workspace entry point, and a call
+    after the first changes neither the device's free memory nor torch's allocation count."""
+    q, k, wq, wk, K = _case(131072, 13)
+    want = native.select_blocks(q, k, wq, wk, K, local_window=0, sink_blocks=1)
+    B, _, T, _ = q.shape
+    out = torch.full((B, k.shape[1], (T + 63) // 64, K), -7, device="cuda", dtype=torch.int32)
+    wq32, wk32 = wq.float().contiguous(), wk.float().contiguous()
+    _noalloc(q, k, wq32, wk32, K, 0, 1, out=out)  # first call on this device: symbol address lookup
+    torch.cuda.synchronize()
+    assert torch.equal(out.cpu(), want.cpu()), "noalloc selection differs at config 2"
+    free0, _ = torch.cuda.mem_get_info()
+    alloc0 = torch.cuda.memory_allocated()
+    out.fill_(-7)
+    _noalloc(q, k, wq32, wk32, K, 0, 1, out=out)
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert torch.cuda.memory_allocated() == alloc0, "torch allocated during the call"
+    assert free1 == free0, f"device free memory changed by {free0 - free1} bytes during the call"
+    assert torch.equal(out.cpu(), want.cpu()), "second noalloc call differs at config 2"
