@@ -64,6 +64,7 @@ SIGNATURES = {
     "spruce_ipc_export": ([_P, _P, ctypes.POINTER(ctypes.c_int64)], _INT),
     "spruce_ipc_import": ([_P, _I64, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p)], _INT),
     "spruce_ipc_close": ([_P], _INT),
+    "spruce_exp2_selfcheck": ([_P, _I64, _P, _P, _P], _INT),
     "spruce_pack_selected_ids": ([_P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P], _INT),
     "spruce_validate_selected_blocks": ([_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P], _INT),
     "spruce_sparse_attention_fwd": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _INT, _I64, _I64, _I64, _I64, _I64,

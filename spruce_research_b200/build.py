@@ -5,10 +5,12 @@
 The library is plain CUDA C++ with an extern "C" interface (include/spruce_b200.h);
 it links the CUDA runtime statically and reaches the driver's tensor-map
 encoder through cudaGetDriverEntryPoint, so it needs nothing but the driver
-at run time.  Rebuilds only when a source is newer than the library.
+at run time.  Rebuilds unless the library was built from exactly the current
+sources, headers and flags (a SHA-256 kept beside it).
 """
 from __future__ import annotations
 
+import hashlib
 import os
 import shutil
 import subprocess
@@ -38,13 +40,26 @@ def nvcc() -> str:
     raise RuntimeError("nvcc not found; install the CUDA toolkit to build libspruce_b200.so")
 
 
+KEY = LIB + ".key"  # SHA-256 of the sources, headers and flags the library was built from
+
+
+def _source_key() -> str:
+    h = hashlib.sha256()
+    deps = [os.path.join(CSRC, f) for f in SOURCES + HEADERS] + [os.path.join(REPO, "include", "spruce_b200.h")]
+    for d in deps:
+        h.update(os.path.basename(d).encode())
+        with open(d, "rb") as f:
+            h.update(f.read())
+    h.update(" ".join(NVCC_FLAGS).encode())
+    return h.hexdigest()
+
+
 def _stale() -> bool:
-    if not os.path.exists(LIB):
+    """The library is rebuilt unless it exists and was built from exactly these sources and flags."""
+    if not os.path.exists(LIB) or not os.path.exists(KEY):
         return True
-    built = os.path.getmtime(LIB)
-    deps = [os.path.join(CSRC, f) for f in SOURCES + HEADERS]
-    deps.append(os.path.join(REPO, "include", "spruce_b200.h"))
-    return any(os.path.getmtime(d) > built for d in deps)
+    with open(KEY) as f:
+        return f.read().strip() != _source_key()
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
@@ -61,6 +76,8 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if verbose:
         sys.stderr.write(proc.stderr)
     os.replace(tmp, LIB)
+    with open(KEY, "w") as f:
+        f.write(_source_key() + "\n")
     return LIB
 
 

@@ -50,8 +50,10 @@ template <> struct Pack2<__half> {
 // polynomial fitted here (iterated weighted least squares on 20001 points for
 // minimal relative error; max relative error 7.6e-5 with fp32 Horner
 // evaluation, against 3.9e-3 = the bf16 precision P is rounded to), and
-// 2^n added to the exponent field.  x is clamped at -126 so the exponent
-// field stays >= 0; callers only pass x <= 8 (lazy rescale) and never -inf.
+// 2^n applied as 2^(n+1) in the exponent field times 0.5 (the product rounds correctly
+// where the result is subnormal, e.g. x = -126, where p(0) < 1 would otherwise land in
+// the subnormal encoding).  x is clamped at -126; callers only pass x <= 8 (lazy
+// rescale) and never -inf.
 __device__ __forceinline__ float poly_exp2(float x) {
   x = fmaxf(x, -126.0f);
   const float kRound = 12582912.0f;  // 1.5 * 2^23
@@ -61,7 +63,7 @@ __device__ __forceinline__ float poly_exp2(float x) {
   const float p =
       fmaf(fmaf(fmaf(0.05517556518316269f, f, 0.24262112379074097f), f, 0.6932611465454102f), f, 0.999927282333374f);
   const int ni = __float_as_int(t) - __float_as_int(kRound);
-  return __int_as_float(__float_as_int(p) + (ni << 23));
+  return __int_as_float(__float_as_int(p) + ((ni + 1) << 23)) * 0.5f;
 }
 
 // Packed fp32 pairs (sm_100 f32x2 instructions: two lanes of fp32 math per
@@ -82,6 +84,11 @@ __device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
 __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
   uint64_t d;
   asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
 __device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
@@ -111,8 +118,9 @@ __device__ __forceinline__ void poly_exp2_x2(float x0, float x1, float& e0, floa
   float q0, q1, t0, t1;
   f2_unpack(q, q0, q1);
   f2_unpack(t, t0, t1);
-  e0 = __int_as_float(__float_as_int(q0) + ((__float_as_int(t0) - __float_as_int(kRound)) << 23));
-  e1 = __int_as_float(__float_as_int(q1) + ((__float_as_int(t1) - __float_as_int(kRound)) << 23));
+  const float s0 = __int_as_float(__float_as_int(q0) + ((__float_as_int(t0) - __float_as_int(kRound) + 1) << 23));
+  const float s1 = __int_as_float(__float_as_int(q1) + ((__float_as_int(t1) - __float_as_int(kRound) + 1) << 23));
+  f2_unpack(f2_mul(f2_pack(s0, s1), f2_pack(0.5f, 0.5f)), e0, e1);
 }
 
 __device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t (&r)[16]) {

@@ -554,6 +554,29 @@ static cudaError_t launch_pair_typed(const AttnArgs& a, CUtensorMapDataType dt, 
   return cudaGetLastError();
 }
 
+// Self-check of the softmax's two exponentials: poly[i] = poly_exp2_x2 (FMA pipe, as the
+// pair kernel evaluates it), mufu[i] = ex2.approx.ftz (MUFU), both over x[i].
+__global__ void exp2_probe_kernel(const float* x, float* poly, float* mufu, int64_t n) {
+  const int64_t i = 2 * ((int64_t)blockIdx.x * blockDim.x + threadIdx.x);
+  if (i >= n) return;
+  const float x0 = x[i], x1 = i + 1 < n ? x[i + 1] : 0.0f;
+  float e0, e1;
+  poly_exp2_x2(x0, x1, e0, e1);
+  poly[i] = e0;
+  mufu[i] = fast_exp2(x0);
+  if (i + 1 < n) {
+    poly[i + 1] = e1;
+    mufu[i + 1] = fast_exp2(x1);
+  }
+}
+
+cudaError_t launch_exp2_probe(const float* x, float* poly, float* mufu, int64_t n, cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  const int64_t pairs = (n + 1) / 2;
+  exp2_probe_kernel<<<(unsigned)((pairs + 255) / 256), 256, 0, stream>>>(x, poly, mufu, n);
+  return cudaGetLastError();
+}
+
 constexpr size_t kPairMaxSmem = 227 * 1024;
 
 int attn_pair_max_kw(int D) {

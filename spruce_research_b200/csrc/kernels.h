@@ -125,6 +125,8 @@ int attn_sm100_max_kw(int D);
 // Two selected blocks per step (N = 128 QK MMAs); attn_pair_sm100.cu.
 cudaError_t launch_attn_pair(const AttnArgs& a, int dtype, cudaStream_t stream);
 int attn_pair_max_kw(int D);
+// The pair kernel's FMA-pipe polynomial exp2 and the MUFU exp2 over n values (self-check).
+cudaError_t launch_exp2_probe(const float* x, float* poly, float* mufu, int64_t n, cudaStream_t stream);
 
 // K/V summary table of the residual tree (summaries.cu).
 struct KvSummaryArgs {

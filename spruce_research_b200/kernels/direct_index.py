@@ -59,8 +59,13 @@ def kernel_runtime_metadata(kernel_variant):
     """Which kernel serves a variant (reference: autotune choice, :430-448)."""
     if kernel_variant not in KERNEL_VARIANTS:
         raise ValueError(f"kernel_variant must be one of {KERNEL_VARIANTS}, got {kernel_variant!r}")
-    return {
-        "variant": kernel_variant,
-        "best_config": {"kernel": "attn_fwd_sm100_kernel", "tile_rows": 128, "heads_per_tile": 2,
-                        "kv_stages": 4, "threads": 352, "fp32_kernel": "attn_fwd_f32_kernel"},
-    }
+    import os
+
+    if os.environ.get("SPRUCE_ATTN_KERNEL") == "single":  # the one-block-per-step kernel, kept for comparison
+        cfg = {"kernel": "attn_fwd_sm100_kernel", "tile_rows": 128, "heads_per_tile": 2, "tiles_per_cta": 2,
+               "blocks_per_step": 1, "kv_stages": 4, "threads": 352}
+    else:  # the default: two selected blocks per step (attn_pair_sm100.cu)
+        cfg = {"kernel": "attn_pair_sm100_kernel", "tile_rows": 128, "heads_per_tile": 2, "tiles_per_cta": 2,
+               "blocks_per_step": 2, "kv_stages": {64: 4, 128: 2}, "threads": 320}
+    cfg["fp32_kernel"] = "attn_fwd_f32_kernel"
+    return {"variant": kernel_variant, "best_config": cfg}
