@@ -114,7 +114,7 @@ class FlatGate(nn.Module):
 
 def load_gate(path, device):
     """Load a gate checkpoint ``{state_dict, config}`` (scripts/eval_tree_traversal.py:26-32)."""
-    ck = torch.load(path, map_location="cpu", weights_only=False)
+    ck = torch.load(path, map_location="cpu", weights_only=True)  # plain tensors and a config dict
     cfg = ck["config"]
     gate = FlatGate(cfg["num_layers"], cfg["head_dim"], cfg["proj_dim"])
     gate.load_state_dict(ck["state_dict"])

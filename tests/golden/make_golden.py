@@ -119,8 +119,8 @@ def big_case(ref, name):
     import time
 
     shape, dtype, seed, wseed, rope, K, lw, sink, keep = BIG_CASES[name]
-    t0 = time.time()
     q, k, v = make_layer_inputs(shape, dtype, seed, rope_theta=rope)
+    t0 = time.perf_counter()
     wq, wk = make_gate_weights(1, shape.head_dim, shape.head_dim, wseed)
     qb = shape.query_blocks
     if K is None:
@@ -139,6 +139,7 @@ def big_case(ref, name):
     selected = torch.empty((B, G, qb, K), dtype=torch.int32)
     gap = torch.full((B, G, qb), float("inf"), dtype=torch.float32)
     floor = torch.finfo(torch.float32).min
+    t_gap = 0.0
     for b in range(B):
         for g in range(G):
             with torch.no_grad():
@@ -148,14 +149,18 @@ def big_case(ref, name):
             sel = ref["pack"](ids, k_selected=K, local_window=lw, key_blocks=qb, sink_blocks=sink)
             ref["validate"](sel, local_window=lw)
             selected[b, g] = sel[0, 0, 0]
+            tg = time.perf_counter()  # the gap bookkeeping is not part of the reference's path
             top = masked[0, 0].topk(min(width + 1, qb), dim=-1).values     # [qb, width + 1]
             if top.shape[-1] > width:
                 real = top[:, width] > floor
                 gap[b, g, real] = (top[real, width - 1] - top[real, width])
+            t_gap += time.perf_counter() - tg
             del s, masked
-    t_sel = time.time() - t0
+    t_sel = time.perf_counter() - t0 - t_gap
+    t1 = time.perf_counter()
     out, _ = ref["attention"](_Module(), q, k, v, None, selected_blocks=selected[:, None].contiguous(),
                               block_size=64, validate_selected_blocks_input=False)
+    t_attn = time.perf_counter() - t1
     rows = torch.cat([torch.arange(i * 64, min((i + 1) * 64, shape.tokens)) for i in keep])
     digest = {}
     for key, t in (("pooled_q", pooled_q), ("pooled_k", pooled_k)):
@@ -170,9 +175,57 @@ def big_case(ref, name):
         pooled_q_sha256=digest["pooled_q"], pooled_k_sha256=digest["pooled_k"],
         selected=selected.to(torch.int16).numpy(), gap=gap.numpy(),
         out=_raw(out[:, rows]), out_blocks=np.array(keep, dtype=np.int64),
+        # Wall time of the reference's own CPU path on the host that made this fixture:
+        # [selector s (pooling, gate, mask / top-k, packing; all KV groups), attention s, torch threads,
+        #  os.cpu_count()].  Measured once, inputs already in memory.
+        ref_cpu=np.array([t_sel, t_attn, torch.get_num_threads(), os.cpu_count() or 0], dtype=np.float64),
     )
-    print(f"{name}: K={K} selector {t_sel:.1f} s, total {time.time() - t0:.1f} s; "
+    print(f"{name}: K={K} selector {t_sel:.1f} s, attention {t_attn:.1f} s; "
           f"smallest boundary gap {gap.min().item():.3e}, rows with gap < 1e-6: {(gap < 1e-6).sum().item()}")
+
+
+# Trained gate weights: the reference's checkpoint (selector_ckpt/<file>, {state_dict, config}),
+# loaded through this repository's load_gate; one gate layer's Wq/Wk are stored.
+TRAINED = ("flat_gate_trained.pt", 13)
+
+
+def trained_case(ref, reference_root):
+    """The reference's flat (P = 1) and tree (P = 8, beam 16) selectors with trained weights.
+
+    Inputs: the config-1 layer shape at 8192 tokens (seed 41).  P = 1: pooled means,
+    FlatGate scores, mask / top-k at 10% density, selected_ids_to_blocks.  P = 8: outlier
+    prototypes of the group-averaged queries and of the keys in fp32, build_key_tree
+    (radix 2) and traverse_to_leaf_ids (beam 16).
+    """
+    from spruce_research_b200.selector.gate import load_gate
+
+    ours, cfg = load_gate(os.path.join(reference_root, "selector_ckpt", TRAINED[0]), "cpu")
+    layer = TRAINED[1]
+    wq, wk = ours.Wq[layer].detach().clone(), ours.Wk[layer].detach().clone()
+    shape, seed = LayerShape(1, 28, 4, 8192, 128), 41
+    q, k, v = make_layer_inputs(shape, torch.bfloat16, seed, rope_theta=1e6)
+    K = k_for_density(shape.query_blocks, 0.10)
+    flat = reference_pipeline(ref, q, k, v, wq, wk, K, 0, 1)
+    q_feat = ref["proto_pool"](ref["group_avg"](q, shape.kv_heads), 64, 8).float()   # [1, G, qb, 8, d]
+    k_feat = ref["proto_pool"](k, 64, 8).float()
+    gate = ref["FlatGate"](1, shape.head_dim, shape.head_dim).eval()
+    with torch.no_grad():
+        gate.Wq.copy_(wq[None])
+        gate.Wk.copy_(wk[None])
+        levels = ref["build_key_tree"](k_feat, radix=2)
+        leaf_ids = ref["traverse"](gate, q_feat, levels, 16, radix=2)
+    np.savez_compressed(
+        os.path.join(HERE, "trained.npz"),
+        checkpoint=np.array([TRAINED[0]]), layer=np.array([layer]),
+        config=np.array([cfg["num_layers"], cfg["head_dim"], cfg["proj_dim"]]),
+        wq=wq.numpy(), wk=wk.numpy(),
+        shape=np.array([shape.batch, shape.q_heads, shape.kv_heads, shape.tokens, shape.head_dim]),
+        seed=np.array([seed]), policy=np.array([K, 0, 1]),
+        checksum=np.array([q.double().sum().item(), k.double().sum().item(), v.double().sum().item()]),
+        selected=flat["selected"].numpy(), leaf_ids=leaf_ids.numpy(),
+    )
+    print(f"trained: {TRAINED[0]} layer {layer}, P=1 selected {tuple(flat['selected'].shape)}, "
+          f"P=8 leaf ids {tuple(leaf_ids.shape)}")
 
 
 def packing_cases(ref):
@@ -352,7 +405,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("SPRUCE_REFERENCE"),
                     help="path of the reference checkout (or set SPRUCE_REFERENCE)")
-    ap.add_argument("--only", choices=["all", "summaries", "maxsim", "residual", "c1_full", "c2"], default="all")
+    ap.add_argument("--only", choices=["all", "summaries", "maxsim", "residual", "c1_full", "c2", "trained"],
+                    default="all")
     args = ap.parse_args()
     if not args.reference:
         ap.error("give --reference (or SPRUCE_REFERENCE): the reference checkout to run")
@@ -385,6 +439,9 @@ def main():
         return
     if args.only in BIG_CASES:
         big_case(ref, args.only)
+        return
+    if args.only == "trained":
+        trained_case(ref, args.reference)
         return
 
     for name, (shape, dtype, seed, rope, K, lw, sink, keep_blocks) in CASES.items():
@@ -420,6 +477,7 @@ def main():
     np.savez_compressed(os.path.join(HERE, "residual.npz"), **residual_cases(ref))
     for name in BIG_CASES:
         big_case(ref, name)
+    trained_case(ref, args.reference)
     print("wrote", sorted(f for f in os.listdir(HERE) if f.endswith(".npz")))
 
 

@@ -135,3 +135,24 @@ def test_residual_summary_keyword_errors_follow_reference():
         sparse_prefill_attention_forward(_Module(), query, key, value, None, residual_summaries=True,
                                          residual_summary_nodes=nodes, summary_mode="learned",
                                          summary_checkpoint="ckpt.pt", **args)
+
+
+def test_load_gate_reads_the_reference_checkpoint_format_without_unpickling_code(tmp_path):
+    """{state_dict: {Wq, Wk}, config: {num_layers, head_dim, proj_dim}}, as the reference's
+    selector_ckpt/*.pt files hold (scripts/eval_tree_traversal.py:26-32), loaded with
+    torch.load(weights_only=True): plain tensors and a dict only."""
+    import pickle
+    from fractions import Fraction  # an arbitrary class a weights_only load refuses to unpickle
+
+    from spruce_research_b200.selector.gate import load_gate
+
+    wq, wk = torch.randn(2, 8, 4), torch.randn(2, 8, 4)
+    path = tmp_path / "gate.pt"
+    torch.save({"state_dict": {"Wq": wq, "Wk": wk}, "config": {"num_layers": 2, "head_dim": 8, "proj_dim": 4}}, path)
+    gate, cfg = load_gate(str(path), "cpu")
+    assert cfg == {"num_layers": 2, "head_dim": 8, "proj_dim": 4}
+    assert torch.equal(gate.Wq, wq) and torch.equal(gate.Wk, wk)
+    bad = tmp_path / "bad.pt"
+    torch.save({"state_dict": {"Wq": wq, "Wk": wk}, "config": Fraction(1, 3)}, bad)
+    with pytest.raises(pickle.UnpicklingError):
+        load_gate(str(bad), "cpu")

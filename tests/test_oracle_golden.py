@@ -115,7 +115,8 @@ def test_golden_fixtures_are_small():
     from golden_cases import HERE
 
     total = sum(os.path.getsize(os.path.join(HERE, f)) for f in os.listdir(HERE) if f.endswith(".npz"))
-    assert total < 8 * 2**20
+    # the headline configurations (c1_full, c2) carry their whole selected_blocks and sampled attention rows
+    assert total < 12 * 2**20
     assert np.load(os.path.join(HERE, "c0.npz"))["selected"].dtype == np.int32
 
 
@@ -252,3 +253,42 @@ def test_headline_attention_rows_match_reference(name):
     # the reference's output is rounded to bf16: within one ulp of |x| <= 8
     assert err.max().item() < 1.6e-2
     assert err.mean().item() < 1e-3
+
+
+# ---------------------------------------------------------------- trained gate weights
+def trained_case():
+    """(fixture, q, k, wq, wk, same): the reference's selections with one layer of its trained
+    checkpoint (tests/golden/trained.npz), the regenerated inputs they were made on, and
+    whether this host regenerated exactly those inputs."""
+    from spruce_research_b200.synthetic import LayerShape, make_layer_inputs
+
+    z = load_npz("trained")
+    B, Hq, Hkv, T, D = (int(x) for x in z["shape"])
+    q, k, v = make_layer_inputs(LayerShape(B, Hq, Hkv, T, D), torch.bfloat16, int(z["seed"][0]), rope_theta=1e6)
+    cs = np.array([q.double().sum().item(), k.double().sum().item(), v.double().sum().item()])
+    return z, q, k, torch.from_numpy(z["wq"]), torch.from_numpy(z["wk"]), bool(np.allclose(cs, z["checksum"]))
+
+
+def test_trained_gate_flat_selection_matches_reference():
+    z, q, k, wq, wk, same = trained_case()
+    assert same, "synthetic generator drifted"
+    K, lw, sink = (int(x) for x in z["policy"])
+    got = O.select_blocks(q, k, wq, wk, K, lw, sink)["selected"]
+    assert torch.equal(got, torch.from_numpy(z["selected"]))
+
+
+def test_trained_gate_tree_traversal_matches_reference():
+    from spruce_research_b200.selector.tree import _level_ranges
+
+    z, q, k, wq, wk, same = trained_case()
+    assert same, "synthetic generator drifted"
+    G = k.shape[1]
+    qf = O.proto_pool_seq(O.group_avg_tokens(q, G), 64, 8)[0].float()   # [G, qb, 8, d]
+    level = O.proto_pool_seq(k, 64, 8)[0].float()
+    levels = [level]
+    while level.shape[1] > 1:
+        level = O.tree_merge(level)
+        levels.append(level)
+    starts = [torch.tensor(s) for s, _ in _level_ranges(qf.shape[1], 2)]
+    ids = O.traverse_to_leaf_ids(O.project(qf, wq), [O.project(x, wk) for x in levels], starts, beam=16)
+    assert torch.equal(ids, torch.from_numpy(z["leaf_ids"])[0])
