@@ -283,6 +283,23 @@ def headline_fixture(args, shape, K):
     return z
 
 
+def reference_cpu_record(fixture, flops: float):
+    """The reference's own CPU torch path at this workload, as timed where the fixture was made.
+
+    tests/golden/make_golden.py runs the reference's functions (pooling, FlatGate, mask and
+    top-k, selected_ids_to_blocks, sparse_prefill_attention_forward) on these inputs and
+    stores their wall time; the reference checkout itself does not travel to the GPU box.
+    """
+    if fixture is None or "ref_cpu" not in fixture.files:
+        return None
+    t_sel, t_attn, threads, cpus = (float(x) for x in fixture["ref_cpu"])
+    return {"value": flops / (t_sel + t_attn) / 1e12, "unit": "TFLOP/s", "seconds_per_layer": t_sel + t_attn,
+            "selector_s": t_sel, "attention_s": t_attn, "torch_threads": int(threads), "cpu_count": int(cpus),
+            "kind": "reference",
+            "where": ("the reference's own torch functions, whole layer (all 4 KV groups, every query block), timed "
+                      "by tests/golden/make_golden.py on the host that generated the fixtures, not on this box")}
+
+
 def attention_error(got, want) -> dict:
     err = (got.float().cpu() - want.float().cpu()).abs()
     return {"max_abs": err.max().item(), "mean_abs": err.mean().item()}
@@ -467,6 +484,9 @@ def run_b200(args):
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         cpu, _, checked = cpu_sample(shape, K, q_host, k_host, v_host, wq[0], wk[0], args.cpu_seconds)
+        ref_rec = reference_cpu_record(fixture, flops)
+        if ref_rec is not None:
+            cpu["reference_torch_path"] = ref_rec
         c0, c1 = checked["blocks"]
         parity["oracle"] = {"rows_equal": int((sel_buf[:, 0].cpu() == checked["selected_g0"]).all(-1).sum()),
                             "rows_total": qb, "kv_group": 0, "query_blocks": [c0, c1],
@@ -546,8 +566,14 @@ def run_reference(args):
         "config": config_dict(args, shape, K, entries, args.gpus),
         "cpu_baseline": {**info, "value": value},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "note": "ms_per_step extrapolates the sample's rate to the whole layer",
+        "note": ("ms_per_step extrapolates the sample's rate to the whole layer; the reference's Python checkout "
+                 "cannot run on this box, so this arm times the C restatement of its path (kind 'port'); "
+                 "cpu_baseline.reference_torch_path is the reference's own torch path timed where the fixtures "
+                 "were made"),
     }
+    ref_rec = reference_cpu_record(headline_fixture(args, shape, K), flops)
+    if ref_rec is not None:
+        result["cpu_baseline"]["reference_torch_path"] = ref_rec
     emit(result)
 
 
