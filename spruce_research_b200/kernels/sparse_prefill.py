@@ -25,12 +25,12 @@ def selected_blocks_to_block_mask(selected_blocks, *, layer_idx, num_query_heads
         raise ValueError(f"layer_idx {layer_idx} is outside selected_blocks layers={L}")
     if num_query_heads % Gkv:
         raise ValueError("num_query_heads must be divisible by selected KV groups")
-    rows = selected_blocks[:, layer_idx].to(torch.long)
-    valid = (rows >= 0) & (rows < qblocks)
-    ids = rows.clamp(min=0, max=qblocks - 1).masked_fill(~valid, qblocks)   # padding -> spare column
-    mask = torch.zeros((B, Gkv, qblocks, qblocks + 1), device=rows.device, dtype=torch.bool)
-    mask.scatter_(-1, ids, True)
-    return mask[..., :qblocks].repeat_interleave(num_query_heads // Gkv, dim=1).contiguous()
+    # mask[b, h, i, j] holds when block j is one of row i's ids in head h's KV group; -1 padding
+    # and ids outside [0, Qb) equal no block column, so they mark nothing.
+    rows = selected_blocks[:, layer_idx].to(torch.long)                        # [B, Gkv, Qb, K]
+    blocks = torch.arange(qblocks, device=rows.device)
+    mask = (rows[..., :, None] == blocks).any(dim=-2)                          # [B, Gkv, Qb, Qb]
+    return mask.repeat_interleave(num_query_heads // Gkv, dim=1).contiguous()
 
 
 def selected_blocks_to_head_indices(selected_blocks, *, layer_idx, num_query_heads):

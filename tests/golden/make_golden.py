@@ -228,6 +228,48 @@ def trained_case(ref, reference_root):
           f"P=8 leaf ids {tuple(leaf_ids.shape)}")
 
 
+# The whole model at sparse density: a tiny random Qwen2 (tests/golden_cases.py LIVE_MODEL) run
+# with the reference's own torch attention backend on fixed routes at ~10% density.
+LIVE = dict(model_seed=11, ids_seed=3, tokens=64 * 64 + 17, routes_seed=17)
+
+
+def live_case(reference_root):
+    """Logits of the last token, the final hidden states and every layer's output at sampled
+    token rows, from the reference's registered backend (sparse/attention.py:277-291,
+    sparse_prefill_attention_forward) in a transformers Qwen2 given selected_blocks."""
+    sys.path.insert(0, os.path.join(REPO, "tests"))
+    from golden_cases import LIVE_MODEL, live_rows, model_checksum, tiny_qwen2
+    from scripts.export_selected_blocks import selected_ids_to_blocks
+    from interfaces.validator import validate_selected_blocks
+    from sparse.attention import register_sparse_prefill_attention
+
+    T = LIVE["tokens"]
+    model = tiny_qwen2(LIVE["model_seed"])
+    ids = torch.randint(0, LIVE_MODEL["vocab_size"], (1, T), generator=torch.Generator().manual_seed(LIVE["ids_seed"]))
+    L, G = LIVE_MODEL["num_hidden_layers"], LIVE_MODEL["num_key_value_heads"]
+    qb = (T + 63) // 64
+    K = k_for_density(qb, 0.10)
+    cand = torch.randint(0, qb, (L, G, qb, K), generator=torch.Generator().manual_seed(LIVE["routes_seed"]))
+    routes = selected_ids_to_blocks(cand, K, local_window=0, key_blocks=qb, sink_blocks=1)   # [1, L, G, qb, K]
+    validate_selected_blocks(routes, local_window=0)
+    model.set_attn_implementation(register_sparse_prefill_attention())
+    with torch.no_grad():
+        out = model.base_model(ids, use_cache=False, selected_blocks=routes, block_size=64,
+                               validate_selected_blocks_input=False, output_hidden_states=True)
+        final = out.last_hidden_state
+        logits = model.get_output_embeddings()(final[:, -1:, :])
+    rows = live_rows(T)
+    layers = torch.stack([h[0, rows] for h in out.hidden_states[1:L]])   # outputs of layers 0 .. L-2
+    density = float((routes >= 0).sum()) / (L * G * qb * (qb + 1) / 2)
+    np.savez_compressed(
+        os.path.join(HERE, "live.npz"),
+        seeds=np.array([LIVE["model_seed"], LIVE["ids_seed"], LIVE["routes_seed"]]), tokens=np.array([T]),
+        model_checksum=np.array([model_checksum(model)]), routes=routes.to(torch.int16).numpy(),
+        logits=logits[0, 0].float().numpy(), final_rows=_raw(final[0, rows]), layer_rows=_raw(layers),
+    )
+    print(f"live: T={T}, K={K}, charged density {density:.3f}, logits {tuple(logits.shape)}")
+
+
 def packing_cases(ref):
     gen = torch.Generator().manual_seed(11)
     cases = {}
@@ -405,7 +447,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("SPRUCE_REFERENCE"),
                     help="path of the reference checkout (or set SPRUCE_REFERENCE)")
-    ap.add_argument("--only", choices=["all", "summaries", "maxsim", "residual", "c1_full", "c2", "trained"],
+    ap.add_argument("--only", choices=["all", "summaries", "maxsim", "residual", "c1_full", "c2", "trained",
+                                                   "live"],
                     default="all")
     args = ap.parse_args()
     if not args.reference:
@@ -443,6 +486,9 @@ def main():
     if args.only == "trained":
         trained_case(ref, args.reference)
         return
+    if args.only == "live":
+        live_case(args.reference)
+        return
 
     for name, (shape, dtype, seed, rope, K, lw, sink, keep_blocks) in CASES.items():
         q, k, v = make_layer_inputs(shape, dtype, seed, rope_theta=rope)
@@ -478,6 +524,7 @@ def main():
     for name in BIG_CASES:
         big_case(ref, name)
     trained_case(ref, args.reference)
+    live_case(args.reference)
     print("wrote", sorted(f for f in os.listdir(HERE) if f.endswith(".npz")))
 
 

@@ -237,3 +237,28 @@ def raw_sha256(t: torch.Tensor) -> bytes:
     if t.dtype in (torch.bfloat16, torch.float16):
         t = t.view(torch.int16)
     return hashlib.sha256(t.numpy().tobytes()).digest()
+
+
+# ---------------------------------------------------------------- whole-model case (tests/golden/live.npz)
+LIVE_MODEL = dict(vocab_size=512, hidden_size=512, intermediate_size=1024, num_hidden_layers=3,
+                  num_attention_heads=8, num_key_value_heads=2, max_position_embeddings=8192, rope_theta=1e6)
+
+
+def tiny_qwen2(seed: int, dtype=torch.bfloat16):
+    """A random-init Qwen2 of LIVE_MODEL's shape, initialised on the CPU from `seed` (so every
+    host with the same torch builds the same weights); move it to a device afterwards."""
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+
+    torch.manual_seed(seed)
+    with torch.device("cpu"):
+        model = Qwen2ForCausalLM(Qwen2Config(**LIVE_MODEL)).to(dtype).eval()
+    return model
+
+
+def model_checksum(model) -> float:
+    return float(sum(p.detach().double().sum().item() for p in model.parameters()))
+
+
+def live_rows(T: int) -> torch.Tensor:
+    """Token rows whose hidden states the fixture stores: the first block and the last two."""
+    return torch.cat([torch.arange(0, 64), torch.arange(T - 128, T)])

@@ -144,3 +144,43 @@ def test_dense_layers_reproduce_sdpa_and_decode_runs():
         model.set_attn_implementation("sdpa")
     assert step.logits.shape == (1, 1, 512) and torch.isfinite(step.logits).all()
     assert out.past_key_values.get_seq_length() == T + 1
+
+
+@pytest.mark.gpu
+def test_sparse_density_model_passes_the_reference_acceptance_against_its_own_backend():
+    """A tiny Qwen2 at ~10% block density (K = 4 of 65 query blocks, sink + diagonal + 2
+    routed), on the fixed routes stored with it: this library's drop-in callback against the
+    reference's own torch backend run on the CPU (tests/golden/live.npz), judged by the
+    reference's acceptance criteria (spruce_research_b200.acceptance) on the last token's
+    logits and the final hidden states, and by relative RMSE <= 0.02 on every layer's output."""
+    import numpy as np
+
+    from golden_cases import from_raw, live_rows, load_npz, model_checksum, tiny_qwen2
+    from spruce_research_b200.acceptance import logits_error, passes_acceptance, tensor_error
+    from spruce_research_b200.kernels.sparse_prefill import register_triton_sparse_prefill_attention
+
+    z = load_npz("live")
+    model_seed, ids_seed, _ = (int(x) for x in z["seeds"])
+    T = int(z["tokens"][0])
+    model = tiny_qwen2(model_seed)
+    assert abs(model_checksum(model) - float(z["model_checksum"][0])) <= 1e-9 * abs(float(z["model_checksum"][0]))
+    model = model.cuda()
+    ids = torch.randint(0, 512, (1, T), generator=torch.Generator().manual_seed(ids_seed)).cuda()
+    routes = torch.from_numpy(z["routes"].astype(np.int32)).cuda()
+    model.set_attn_implementation(register_triton_sparse_prefill_attention())
+    try:
+        with torch.no_grad():
+            out = model.base_model(ids, use_cache=False, selected_blocks=routes, block_size=64,
+                                   output_hidden_states=True)
+            final = out.last_hidden_state
+            logits = model.get_output_embeddings()(final[:, -1:, :])
+    finally:
+        model.set_attn_implementation("sdpa")
+    rows = live_rows(T).cuda()
+    lg = logits_error(logits[0, 0].cpu(), torch.from_numpy(z["logits"]))
+    fh = tensor_error(final[0, rows].cpu(), from_raw(z["final_rows"], torch.bfloat16))
+    assert passes_acceptance(lg, fh), {"logits": lg, "final_hidden": fh}
+    want_layers = from_raw(z["layer_rows"], torch.bfloat16)
+    for layer, h in enumerate(out.hidden_states[1:1 + want_layers.shape[0]]):
+        err = tensor_error(h[0, rows].cpu(), want_layers[layer])
+        assert err["relative_rmse"] <= 0.02, (layer, err)

@@ -33,3 +33,18 @@ def test_cu_seqlens_rules():
     with pytest.raises(ValueError, match="exactly one"):
         v.k_for(4096, None, None)
     assert v.k_for(131072, 0.10, None) == 106 and v.k_for(64, None, 1) == 2  # sink + diagonal at least
+
+
+def test_acceptance_criteria_follow_the_reference_definitions():
+    from spruce_research_b200.acceptance import DEFAULT_ACCEPTANCE, logits_error, passes_acceptance, tensor_error
+
+    e = torch.linspace(-3, 3, 512)
+    same = logits_error(e.clone(), e)
+    assert same["cosine"] > 0.999999 and same["top1_same"] and same["top10_overlap"] == 1.0
+    assert tensor_error(e, e)["relative_rmse"] == 0.0
+    assert passes_acceptance(same, tensor_error(e, e))
+    swapped = e.clone()
+    swapped[[-1, 0]] = swapped[[0, -1]]                       # the top-1 token changes
+    assert not passes_acceptance(logits_error(swapped, e), tensor_error(e, e))
+    assert not passes_acceptance(same, tensor_error(e * 1.05, e))   # 5% relative RMSE > 0.02
+    assert DEFAULT_ACCEPTANCE["minimum_logits_cosine"] == 0.999
