@@ -81,6 +81,8 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-chunks", type=int, default=16, help="query-block chunks of the streamed e2e step")
+    ap.add_argument("--e2e-schedule", choices=("balanced", "equal"), default="balanced",
+                    help="chunk bounds of the streamed e2e step: equal attention work or equal query blocks")
     ap.add_argument("--cpu-seconds", type=float, default=24.0, help="target length of one CPU sample")
     ap.add_argument("--gather", choices=("fused", "nccl"), default="fused",
                     help="N>1 output all-gather: NVLink peer stores in the attention epilogue, or NCCL")
@@ -425,7 +427,7 @@ def run_b200(args):
         dq, dk, dv = (torch.empty_like(t, device=dev) for t in (hq, hk, hv))
         # each rank reads back the rows and heads it computed: over all ranks, the whole output
         hout = torch.empty((B, T, (g1 - g0) * rep, D), dtype=torch.bfloat16).pin_memory()
-        streamer = HostStreamedLayer(layer, dev, chunks=args.e2e_chunks)
+        streamer = HostStreamedLayer(layer, dev, chunks=args.e2e_chunks, schedule=args.e2e_schedule)
 
         def e2e_step():
             # H2D of chunk c+1, selector + attention of chunk c and D2H of chunk c-1 overlap
@@ -452,7 +454,8 @@ def run_b200(args):
         e2e = {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
                "h2d_bytes_per_step": int(moved[0].item()), "d2h_bytes_per_step": int(moved[1].item()),
                "path": ("pinned host Q/K/V -> HostStreamedLayer (copies of chunk c+1, selector + attention of "
-                        f"chunk c and copy-back of chunk c-1 overlap; {args.e2e_chunks} query-block chunks) -> "
+                        f"chunk c and copy-back of chunk c-1 overlap; {args.e2e_chunks} query-block chunks, "
+                        f"{args.e2e_schedule} schedule) -> "
                         "pinned host output" + ("" if world == 1 else
                                                 "; each rank copies its own query rows, the K/V rows they "
                                                 "attend and its output shard (bytes summed over ranks)"))}

@@ -12,6 +12,8 @@ kernels/sparse_prefill.py:55-97 (attention callback).
 """
 from __future__ import annotations
 
+import math
+
 import torch
 
 from . import native
@@ -62,6 +64,24 @@ def _nbytes(t: torch.Tensor) -> int:
     return t.numel() * t.element_size()
 
 
+def chunk_bounds(r0: int, r1: int, chunks: int, schedule: str = "balanced") -> list[int]:
+    """Strictly increasing query-block bounds r0 = b_0 < ... < b_C = r1, C <= chunks.
+
+    "equal": the same number of query blocks per chunk.  "balanced": the same
+    causal attention work per chunk (bound c at sqrt(r0^2 + (r1^2 - r0^2) c / C)).
+    """
+    C = max(1, min(chunks, r1 - r0))
+    if schedule == "equal":
+        return [r0 + (r1 - r0) * c // C for c in range(C + 1)]
+    bounds = [r0]
+    for c in range(1, C):
+        b = int(round(math.sqrt(r0 * r0 + (r1 * r1 - r0 * r0) * c / C)))
+        if bounds[-1] < b < r1:
+            bounds.append(b)
+    bounds.append(r1)
+    return bounds
+
+
 class HostStreamedLayer:
     """One layer fed from pinned host buffers, pipelined over query-block chunks.
 
@@ -74,11 +94,20 @@ class HostStreamedLayer:
 
     ``after_attention(i0, i1)`` runs on the compute stream after each
     chunk's attention (the multi-GPU fence of the fused output all-gather).
+
+    ``schedule="balanced"`` (default) places the chunk bounds so that every
+    chunk holds the same causal attention work (work up to query block i
+    grows as i^2, so bound c sits at sqrt(r0^2 + (r1^2 - r0^2) c / C)): the
+    last chunk, whose compute and copy-back nobody overlaps, stays short.
+    ``schedule="equal"`` gives every chunk the same number of query blocks.
     """
 
-    def __init__(self, layer: SparsePrefillLayer, device, chunks: int = 8):
+    def __init__(self, layer: SparsePrefillLayer, device, chunks: int = 16, schedule: str = "balanced"):
+        if schedule not in ("balanced", "equal"):
+            raise ValueError(f"unknown chunk schedule {schedule!r}")
         self.layer = layer
         self.chunks = chunks
+        self.schedule = schedule
         self.h2d = torch.cuda.Stream(device)
         self.compute = torch.cuda.Stream(device)
         self.d2h = torch.cuda.Stream(device)
@@ -98,8 +127,8 @@ class HostStreamedLayer:
         Hkv = hk.shape[2]
         qb = (T + BLOCK - 1) // BLOCK
         r0, r1 = (0, qb) if q_blocks is None else q_blocks
-        C = max(1, min(self.chunks, r1 - r0))
-        bounds = [r0 + (r1 - r0) * c // C for c in range(C + 1)]
+        bounds = chunk_bounds(r0, r1, self.chunks, self.schedule)
+        C = len(bounds) - 1
         dev = dq.device
         if self._sel is None or self._sel.shape != (B, Hkv, qb, self.layer.k_selected) or self._sel.device != dev:
             self._sel = torch.empty((B, Hkv, qb, self.layer.k_selected), device=dev, dtype=torch.int32)

@@ -16,8 +16,9 @@ from spruce_research_b200.synthetic import LayerShape, k_for_density, make_gate_
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("tokens,chunks", [(8192, 4), (8192 + 100, 3), (2048, 8)])
-def test_streamed_layer_equals_one_shot_layer(tokens, chunks):
+@pytest.mark.parametrize("tokens,chunks,schedule", [(8192, 4, "equal"), (8192 + 100, 3, "balanced"),
+                                                    (2048, 8, "equal"), (8192, 16, "balanced")])
+def test_streamed_layer_equals_one_shot_layer(tokens, chunks, schedule):
     shape = LayerShape(1, 28, 4, tokens, 128)
     K = k_for_density(shape.query_blocks, 0.10)
     q, k, v = make_layer_inputs(shape, torch.bfloat16, seed=21)
@@ -28,7 +29,8 @@ def test_streamed_layer_equals_one_shot_layer(tokens, chunks):
     dq, dk, dv = (torch.empty_like(t, device="cuda") for t in (hq, hk, hv))
     dout = torch.empty_like(want)
     hout = torch.empty(want.shape, dtype=want.dtype).pin_memory()
-    HostStreamedLayer(layer, torch.device("cuda"), chunks=chunks)(hq, hk, hv, dq, dk, dv, dout, hout=hout)
+    streamed = HostStreamedLayer(layer, torch.device("cuda"), chunks=chunks, schedule=schedule)
+    streamed(hq, hk, hv, dq, dk, dv, dout, hout=hout)
     torch.cuda.synchronize()
     assert torch.equal(dout, want)
     assert torch.equal(hout, want.cpu())

@@ -130,3 +130,19 @@ def test_balanced_split_equalises_selected_tiles():
             s = plan(world, r, 4, qb, k_selected=K)
             seen[s.groups[0]:s.groups[1], s.q_blocks[0]:s.q_blocks[1]] += 1
         assert torch.equal(seen, torch.ones_like(seen))
+
+
+@pytest.mark.parametrize("r0,r1,chunks", [(0, 2048, 16), (1024, 2048, 16), (0, 3, 16), (5, 6, 4), (7, 300, 9)])
+def test_chunk_bounds_cover_the_rows_in_order(r0, r1, chunks):
+    from spruce_research_b200.pipeline import chunk_bounds
+    for schedule in ("balanced", "equal"):
+        b = chunk_bounds(r0, r1, chunks, schedule)
+        assert b[0] == r0 and b[-1] == r1 and len(b) - 1 <= chunks
+        assert all(x < y for x, y in zip(b, b[1:]))
+    # balanced: every chunk carries about the same causal work (sum of its query blocks' key counts)
+    b = chunk_bounds(0, 2048, 16)
+    work = [(y * y - x * x) for x, y in zip(b, b[1:])]
+    assert max(work) / min(work) < 1.02   # bounds are whole query blocks
+    with pytest.raises(ValueError):
+        from spruce_research_b200.pipeline import HostStreamedLayer
+        HostStreamedLayer(None, "cpu", schedule="fifo")
