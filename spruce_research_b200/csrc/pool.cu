@@ -8,10 +8,12 @@
 //                  where c_k is the in-order fp32 sum of rows 16k..16k+15
 // (torch's CPU sum over the 64-row axis accumulates 16-row chunks).
 //
-// Layout / roofline: one CTA per (batch, head-or-group, 64-token block) reads
-// the block's rows once with 16-byte vector loads (coalesced along D) and
-// writes one pooled row.  The kernel is HBM-bound: at config 2 it reads Q
-// (0.94 GB) and K (0.13 GB) once and writes 8.4 MB.
+// Layout / roofline: every input row is read once with 16-byte vector loads
+// (coalesced along D) and each 64-token block writes one pooled row (P = 1).
+// At config 2 that is Q (0.94 GB) and K (0.13 GB) read once and 8.4 MB written:
+// an HBM-bound job.  P = 1 runs pool_rows_kernel (one thread per 16-row chunk
+// and 16-byte vector, sums in registers); prototypes (P > 1) need every row of
+// the block at once and run pool_block_kernel (rows staged in shared memory).
 #include <algorithm>
 
 #include "common.cuh"
@@ -191,6 +193,157 @@ __global__ void __launch_bounds__(256) group_avg_kernel(const T* x, int64_t sb, 
   }
 }
 
+// ---------------------------------------------------------------------------
+// P = 1 pooling with one thread per (16-row chunk, 16-byte vector) of a block.
+//
+// A thread sums the group averages of its chunk's rows in registers straight
+// from the loads; only the four chunk partials of a block pass through shared
+// memory.  The rounding points are pool_block_kernel's (and the reference's):
+// the group average rounded to T per element, in-order 16-row chunk sums with
+// pad rows adding +0, chunk totals in order, round, divide by the row count.
+// Two exact shortcuts drop instructions the kernel was bound by:
+//   rep = 1:   x / 1 = x, and x is already a T value (no division, no rounding);
+//   rep = 2^k: x / rep = x * 2^-k (both are the correctly rounded image of the
+//              same real number).
+// Measured before: the per-element division and the 32 KB rows round trip kept
+// pool_block_kernel at ~52% issue-active and 3.7 TB/s.
+
+constexpr int kRowsThreads = 256;
+
+// Group average of one token row's 16-byte vector: heads h = 0..rep-1 at p + h*sh.
+template <typename T, int REP>  // REP = 0: head count known at run time only
+__device__ __forceinline__ void group_vec(const T* p, int64_t sh, int rep, float (&g)[Vec16<T>::N]) {
+  constexpr int VN = Vec16<T>::N;
+  float acc[VN];
+#pragma unroll
+  for (int k = 0; k < VN; ++k) acc[k] = 0.0f;
+  if constexpr (REP > 0) {
+    uint4 raw[REP];
+#pragma unroll
+    for (int h = 0; h < REP; ++h) raw[h] = __ldg(reinterpret_cast<const uint4*>(p + h * sh));
+#pragma unroll
+    for (int h = 0; h < REP; ++h) {
+      const T* e = reinterpret_cast<const T*>(&raw[h]);
+#pragma unroll
+      for (int k = 0; k < VN; ++k) acc[k] = __fadd_rn(acc[k], Elem<T>::to_f(e[k]));
+    }
+    if constexpr (REP == 1) {
+#pragma unroll
+      for (int k = 0; k < VN; ++k) g[k] = acc[k];  // 0 + x: the reference's -0 -> +0 is kept
+    } else if constexpr ((REP & (REP - 1)) == 0) {
+#pragma unroll
+      for (int k = 0; k < VN; ++k) g[k] = round_through<T>(__fmul_rn(acc[k], 1.0f / REP));
+    } else {
+#pragma unroll
+      for (int k = 0; k < VN; ++k) g[k] = round_through<T>(__fdiv_rn(acc[k], static_cast<float>(REP)));
+    }
+  } else {
+    for (int h = 0; h < rep; ++h) {
+      float e[VN];
+      load_vec<T>(p + h * sh, e);
+#pragma unroll
+      for (int k = 0; k < VN; ++k) acc[k] = __fadd_rn(acc[k], e[k]);
+    }
+#pragma unroll
+    for (int k = 0; k < VN; ++k) g[k] = round_through<T>(__fdiv_rn(acc[k], static_cast<float>(rep)));
+  }
+}
+
+// In-order sum over the chunk's 16 rows (rows >= nrows are pad rows and add +0).
+// Rows go U at a time, so that a thread keeps U * max(REP, 1) loads in flight:
+// one row already carries REP >= 4 loads, a single head needs 8 rows.
+template <typename T, int REP>
+__device__ __forceinline__ void chunk_sum(const T* p, int64_t sh, int64_t st, int nrows, int rep,
+                                          float (&s)[Vec16<T>::N]) {
+  constexpr int VN = Vec16<T>::N;
+  constexpr int U = REP == 1 ? 8 : (REP == 2 ? 4 : 1);
+#pragma unroll 1
+  for (int r0 = 0; r0 < 16; r0 += U) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int r = r0 + u;
+      float g[VN];
+      if (r < nrows) {
+        group_vec<T, REP>(p + r * st, sh, rep, g);
+      } else {
+#pragma unroll
+        for (int k = 0; k < VN; ++k) g[k] = 0.0f;
+      }
+#pragma unroll
+      for (int k = 0; k < VN; ++k) s[k] = __fadd_rn(s[k], g[k]);
+    }
+  }
+}
+
+// items = (batch, block, slot) with the slots of one block adjacent (slot s <
+// j0.hout is job 0's head s, the rest job 1's); each CTA takes `ipc` items of
+// 4 * (D / VN) threads.
+template <typename T>
+__global__ void __launch_bounds__(kRowsThreads, 3) pool_rows_kernel(PoolJob j0, PoolJob j1, int njobs, int T_len,
+                                                                  int D, int nb, int nbmax, int slots, int64_t items,
+                                                                  int ipc) {
+  constexpr int VN = Vec16<T>::N;
+  __shared__ __align__(16) float part[kRowsThreads * VN];
+  const int nvec = D / VN;
+  const int per_item = 4 * nvec;
+  const int t = threadIdx.x;
+  const int it = t / per_item;
+  const int w = t - it * per_item;
+  const int c = w / nvec;
+  const int v = w - c * nvec;
+  const int64_t item = (int64_t)blockIdx.x * ipc + it;
+
+  bool active = item < items;
+  int y = 0, b = 0, i = 0, count = 0;
+  bool second = false;  // the item belongs to job 1 (fields are selected by value: no local copy of the jobs)
+  float s[VN];
+#pragma unroll
+  for (int k = 0; k < VN; ++k) s[k] = 0.0f;
+  if (active) {
+    const int slot = static_cast<int>(item % slots);
+    const int64_t rest = item / slots;
+    const int il = static_cast<int>(rest % nbmax);
+    b = static_cast<int>(rest / nbmax);
+    second = njobs > 1 && slot >= j0.hout;
+    y = second ? slot - j0.hout : slot;
+    active = il < (second ? j1.nblk : j0.nblk);
+    if (active) {
+      i = (second ? j1.blk0 : j0.blk0) + il;
+      const int t0 = i * kPoolBlock;
+      count = min(kPoolBlock, T_len - t0);
+      const int rep = second ? j1.rep : j0.rep;
+      const int64_t sh = second ? j1.sh : j0.sh, st = second ? j1.st : j0.st;
+      const int nrows = max(0, min(16, count - 16 * c));
+      const T* p = static_cast<const T*>(second ? j1.x : j0.x) + b * (second ? j1.sb : j0.sb) +
+                   (int64_t)(y * rep) * sh + (int64_t)(t0 + 16 * c) * st + v * VN;
+      switch (rep) {
+        case 1: chunk_sum<T, 1>(p, sh, st, nrows, rep, s); break;
+        case 2: chunk_sum<T, 2>(p, sh, st, nrows, rep, s); break;
+        case 4: chunk_sum<T, 4>(p, sh, st, nrows, rep, s); break;
+        case 7: chunk_sum<T, 7>(p, sh, st, nrows, rep, s); break;
+        case 8: chunk_sum<T, 8>(p, sh, st, nrows, rep, s); break;
+        default: chunk_sum<T, 0>(p, sh, st, nrows, rep, s); break;
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < VN; ++k) part[t * VN + k] = s[k];
+  __syncthreads();
+  if (!active || c != 0) return;
+  // chunk totals in order, round, divide by the real row count
+  T res[VN];
+#pragma unroll
+  for (int k = 0; k < VN; ++k) {
+    float total = 0.0f;
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) total = __fadd_rn(total, part[(t + cc * nvec) * VN + k]);
+    res[k] = Elem<T>::from_f(__fdiv_rn(round_through<T>(total), static_cast<float>(count)));
+  }
+  T* out = static_cast<T*>(second ? j1.out : j0.out) + ((int64_t)(b * (second ? j1.hout : j0.hout) + y) * nb + i) * D +
+           v * VN;
+  *reinterpret_cast<uint4*>(out) = *reinterpret_cast<const uint4*>(res);
+}
+
 template <typename T>
 cudaError_t launch_pool(PoolJob j0, PoolJob j1, int njobs, int B, int T_len, int D, cudaStream_t stream) {
   const int nb = (T_len + kPoolBlock - 1) / kPoolBlock;
@@ -202,7 +355,18 @@ cudaError_t launch_pool(PoolJob j0, PoolJob j1, int njobs, int B, int T_len, int
   }
   const int gx = njobs > 1 ? std::max(j0.nblk, j1.nblk) : j0.nblk;
   if (gx <= 0) return cudaSuccess;
-  dim3 grid(gx, j0.hout + (njobs > 1 ? j1.hout : 0), B);
+  const int slots = j0.hout + (njobs > 1 ? j1.hout : 0);
+  const int per_item = 4 * (D / Vec16<T>::N);
+  if (j0.protos == 1 && (njobs == 1 || j1.protos == 1) && per_item <= kRowsThreads) {
+    const int ipc = kRowsThreads / per_item;
+    const int64_t items = (int64_t)B * gx * slots;
+    const int64_t ctas = (items + ipc - 1) / ipc;
+    if (ctas > INT32_MAX) return cudaErrorInvalidValue;
+    pool_rows_kernel<T><<<(unsigned)ctas, ipc * per_item, 0, stream>>>(j0, j1, njobs, T_len, D, nb, gx, slots,
+                                                                        items, ipc);
+    return cudaGetLastError();
+  }
+  dim3 grid(gx, slots, B);
   pool_block_kernel<T><<<grid, kPoolThreads, smem, stream>>>(j0, j1, njobs, T_len, D, nb);
   return cudaGetLastError();
 }

@@ -57,6 +57,30 @@ def test_pooling_bit_exact_with_reference(name):
         assert torch.equal(pk.cpu(), case.golden("pooled_k")), "pooled K differs from the reference"
 
 
+# group sizes and head dims the reference fixtures do not cover: the exact
+# multiply by 1/8, the run-time group size (3, 5, 6, 16), D = 96 and 256, ragged
+# lengths and batch 2
+POOL_SHAPES = [
+    # (B, Hq, Hkv, T, D, dtype)
+    (2, 24, 8, 1000, 128, torch.bfloat16),   # rep 3
+    (1, 40, 8, 777, 64, torch.float16),      # rep 5
+    (1, 48, 8, 2053, 128, torch.float32),    # rep 6
+    (1, 32, 4, 300, 256, torch.bfloat16),    # rep 8, D = 256
+    (2, 16, 1, 130, 96, torch.bfloat16),     # rep 16, D = 96 (5 blocks of 48 threads per CTA)
+    (1, 8, 2, 200, 256, torch.float32),      # rep 4, D = 256 in fp32 (one block per CTA)
+    (1, 4, 4, 65, 128, torch.float16),       # rep 1: queries pooled per head
+]
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,T,D,dtype", POOL_SHAPES)
+def test_pooling_group_sizes_bit_exact_with_oracle(B, Hq, Hkv, T, D, dtype):
+    q, k, _ = make_layer_inputs(LayerShape(B, Hq, Hkv, T, D), dtype, seed=Hq + T)
+    pq, pk = native.pool_qk(q.cuda(), k.cuda())
+    torch.cuda.synchronize()
+    assert torch.equal(pq.cpu(), O.proto_pool_seq(O.group_avg_tokens(q, Hkv), 64, 1)[:, :, :, 0])
+    assert torch.equal(pk.cpu(), O.proto_pool_seq(k, 64, 1)[:, :, :, 0])
+
+
 @pytest.mark.parametrize("name", CASE_NAMES)
 def test_scores_bit_exact_with_oracle(name):
     case, cpu, (q, k, v, wq, wk), ref, same = _case(name)
