@@ -341,28 +341,19 @@ int spruce_select_blocks_rows(const void* q, const int64_t q_strides[4], const v
   const int k1 = std::max(1, std::min(i1, (int)qb));
   rc = pool_qk_range(q, q_strides, k, k_strides, dtype, B, Hq, Hkv, T, D, pooled_q, pooled_k, i0, i1, k1, stream);
   if (rc) return rc;
+  // both projections in one launch: queries [i0, i1) and keys [0, k1) of every (batch, group)
+  const spruce::ProjRows pj_q{pooled_q, Wq, qp, B * Hkv, (int)qb, i0, i1 - i0};
+  const spruce::ProjRows pj_k{pooled_k, Wk, kp, B * Hkv, (int)qb, 0, k1};
   cudaError_t e;
   switch (dtype) {
     case SPRUCE_DTYPE_F32:
-      e = spruce::launch_project_rows<float>(pooled_q, B * Hkv, (int)qb, i0, i1 - i0, (int)D, Wq, (int)P, qp,
-                                             as_stream(stream));
-      if (e == cudaSuccess)
-        e = spruce::launch_project_rows<float>(pooled_k, B * Hkv, (int)qb, 0, k1, (int)D, Wk, (int)P, kp,
-                                               as_stream(stream));
+      e = spruce::launch_project_pair<float>(pj_q, pj_k, 2, (int)D, (int)P, as_stream(stream));
       break;
     case SPRUCE_DTYPE_BF16:
-      e = spruce::launch_project_rows<__nv_bfloat16>(pooled_q, B * Hkv, (int)qb, i0, i1 - i0, (int)D, Wq, (int)P, qp,
-                                                     as_stream(stream));
-      if (e == cudaSuccess)
-        e = spruce::launch_project_rows<__nv_bfloat16>(pooled_k, B * Hkv, (int)qb, 0, k1, (int)D, Wk, (int)P, kp,
-                                                       as_stream(stream));
+      e = spruce::launch_project_pair<__nv_bfloat16>(pj_q, pj_k, 2, (int)D, (int)P, as_stream(stream));
       break;
     default:
-      e = spruce::launch_project_rows<__half>(pooled_q, B * Hkv, (int)qb, i0, i1 - i0, (int)D, Wq, (int)P, qp,
-                                              as_stream(stream));
-      if (e == cudaSuccess)
-        e = spruce::launch_project_rows<__half>(pooled_k, B * Hkv, (int)qb, 0, k1, (int)D, Wk, (int)P, kp,
-                                                as_stream(stream));
+      e = spruce::launch_project_pair<__half>(pj_q, pj_k, 2, (int)D, (int)P, as_stream(stream));
       break;
   }
   rc = cuda_status(e, "projection launch");

@@ -27,6 +27,18 @@ cudaError_t launch_project(const void* x, int64_t N, int D, const float* W, int 
 template <typename T>
 cudaError_t launch_project_rows(const void* x, int64_t groups, int qb, int row0, int nrows, int D, const float* W,
                                 int P, float* out, cudaStream_t stream);
+// One projection job: rows (n / nrows) * qb + row0 + n % nrows, n < groups * nrows,
+// of x [.., D] (dtype T) times W [D, P] fp32 -> out [.., P] fp32.
+struct ProjRows {
+  const void* x;
+  const float* W;
+  float* out;
+  int64_t groups;
+  int qb, row0, nrows;
+};
+// Up to two projection jobs of the same D and P in one launch.
+template <typename T>
+cudaError_t launch_project_pair(const ProjRows& a, const ProjRows& b, int njobs, int D, int P, cudaStream_t stream);
 
 // Key tree of the deployed selector (tree.cu).
 template <typename T>

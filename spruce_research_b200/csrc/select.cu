@@ -291,6 +291,104 @@ __device__ __forceinline__ void score_rows_async(const float* qs, int qstride, c
   }
 }
 
+// 16 query rows against 512-column slabs with 512 threads: thread t owns rows
+// 8*(t/256)..+7 and the columns j0 + t%256 and j0 + t%256 + 256 (an 8 x 2
+// register tile).  Key projections are staged 16 p at a time by cp.async into
+// two alternating buffers (ks2: 2 x [512][kK16Stride]); query rows are read as
+// broadcast float4s (a warp's lanes share their rows).  Per 4-p step and warp:
+// 8 (q) + 8 (k) shared-memory wavefronts against 16 FMA issue cycles, and 16
+// warps per SM where the 256-thread 4 x 4 tile ran 8 (its 128 KB of keys allow
+// one CTA per SM) and stalled on dependent fmas.  Every score is still one fma
+// chain over p = 0..P-1 in order, so the scores are bit-identical to
+// score_rows_async / score_columns.  Needs P % 4 == 0.
+constexpr int kSelThreads16 = 512;
+constexpr int kSlab16 = 512;
+constexpr int kP16 = 16;
+constexpr int kK16Stride = 20;  // 80-byte rows: the 16-byte loads of 8 consecutive lanes cover all 32 banks
+
+template <typename Emit>
+__device__ __forceinline__ void score_rows16_async(const float* qs, int qstride, const float* __restrict__ kp, int P,
+                                                   int ncols, float* ks2, float denom, Emit emit) {
+  const int t = threadIdx.x;
+  const int rg = t >> 8;
+  const int ct = t & 255;
+  const int npc = (P + kP16 - 1) / kP16;
+  const int total = ((ncols + kSlab16 - 1) / kSlab16) * npc;
+  if (total == 0) return;
+  auto issue = [&](int st) {
+    const int j0 = (st / npc) * kSlab16, p0 = (st % npc) * kP16;
+    float* buf = ks2 + (st & 1) * (kSlab16 * kK16Stride);
+#pragma unroll
+    for (int i = 0; i < kSlab16 * (kP16 / 4) / kSelThreads16; ++i) {
+      const int e = t + kSelThreads16 * i;
+      const int jj = e >> 2, part = e & 3;
+      const int j = j0 + jj, p = p0 + part * 4;
+      const bool ok = j < ncols && p < P;
+      cp_async16(buf + jj * kK16Stride + part * 4, ok ? kp + (int64_t)j * P + p : kp, ok ? 16 : 0);
+    }
+    cp_async_commit();
+  };
+  issue(0);
+  const float* qrow = qs + 8 * rg * qstride;
+  float acc[8][2];
+#pragma unroll
+  for (int r = 0; r < 8; ++r) acc[r][0] = acc[r][1] = 0.0f;
+  for (int st = 0; st < total; ++st) {
+    if (st + 1 < total) {
+      issue(st + 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const float* ks = ks2 + (st & 1) * (kSlab16 * kK16Stride);
+    const int pc = st % npc;
+    const int p0 = pc * kP16;
+    const int pn = min(kP16, P - p0);
+    for (int pp = 0; pp < pn; pp += 4) {
+      const float4 k0 = *reinterpret_cast<const float4*>(ks + ct * kK16Stride + pp);
+      const float4 k1 = *reinterpret_cast<const float4*>(ks + (ct + 256) * kK16Stride + pp);
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const float4 qv = *reinterpret_cast<const float4*>(qrow + r * qstride + p0 + pp);
+        acc[r][0] = __fmaf_rn(qv.x, k0.x, acc[r][0]);
+        acc[r][1] = __fmaf_rn(qv.x, k1.x, acc[r][1]);
+        acc[r][0] = __fmaf_rn(qv.y, k0.y, acc[r][0]);
+        acc[r][1] = __fmaf_rn(qv.y, k1.y, acc[r][1]);
+        acc[r][0] = __fmaf_rn(qv.z, k0.z, acc[r][0]);
+        acc[r][1] = __fmaf_rn(qv.z, k1.z, acc[r][1]);
+        acc[r][0] = __fmaf_rn(qv.w, k0.w, acc[r][0]);
+        acc[r][1] = __fmaf_rn(qv.w, k1.w, acc[r][1]);
+      }
+    }
+    if (pc == npc - 1) {
+      const int j0 = (st / npc) * kSlab16;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int j = j0 + ct + 256 * c;
+        if (j < ncols)
+#pragma unroll
+          for (int r = 0; r < 8; ++r) emit(8 * rg + r, j, __fdiv_rn(acc[r][c], denom));
+      }
+#pragma unroll
+      for (int r = 0; r < 8; ++r) acc[r][0] = acc[r][1] = 0.0f;
+    }
+    __syncthreads();  // buffer st & 1 is refilled by the issue at the top of iteration st + 1
+  }
+}
+
+// Threads and staging floats of select_kernel: 512 threads and two
+// [512][kK16Stride] slabs for 16-row tiles; 256 threads and two [256][kKStride]
+// slabs for 8-row tiles, one for smaller tiles.  After the scores the staging
+// holds the selection's per-warp histograms ([warps][256] ints).
+__host__ __device__ constexpr int select_threads(int rows) { return rows >= 16 ? kSelThreads16 : kScoreThreads; }
+__host__ __device__ constexpr int select_stage_floats(int rows) {
+  return rows >= 16 ? 2 * kSlab16 * kK16Stride : (rows >= 8 ? 2 : 1) * kScoreThreads * kKStride;
+}
+static_assert(select_stage_floats(16) >= select_threads(16) / 32 * 256 &&
+                  select_stage_floats(4) >= select_threads(4) / 32 * 256,
+              "the histograms fit in the staging");
+
 // Full score matrix (FlatGate.forward, P = 1): grid (ceil(qb/ROWS), R).
 template <int ROWS>
 __global__ void __launch_bounds__(kScoreThreads) scores_kernel(const float* __restrict__ qp,
@@ -376,15 +474,16 @@ __device__ __forceinline__ uint32_t warp_radix_select(const uint32_t* keys, int 
 }
 
 template <int ROWS>
-__global__ void __launch_bounds__(kScoreThreads) select_kernel(SelectArgs a) {
+__global__ void __launch_bounds__(select_threads(ROWS), ROWS >= 16 ? 1 : 2) select_kernel(SelectArgs a) {
+  constexpr int NT = select_threads(ROWS);
   extern __shared__ float sm[];
   const int P = a.P;
   const int qb = a.qb;
   const int qstride = (P + 3) / 4 * 4 + 4;           // padded row stride of qs (16-byte aligned rows)
   float* qs = sm;                                   // [ROWS][qstride]
   float* kT = qs + ROWS * qstride;                  // staging: [256][kKStride] or [kPChunk][256]
-  int* hist = reinterpret_cast<int*>(kT + (ROWS >= 8 ? 2 : 1) * kScoreThreads * kKStride);  // [8 warps][256]
-  uint32_t* keys = reinterpret_cast<uint32_t*>(hist + 8 * 256);     // [ROWS][qb]
+  int* hist = reinterpret_cast<int*>(kT);          // [NT / 32 warps][256], once the scores are done
+  uint32_t* keys = reinterpret_cast<uint32_t*>(kT + select_stage_floats(ROWS));  // [ROWS][qb]
 
   const int tiles = (a.q_end - a.q_begin + ROWS - 1) / ROWS;
   const int tile = tiles - 1 - blockIdx.x;          // heavy (late) rows first
@@ -393,22 +492,23 @@ __global__ void __launch_bounds__(kScoreThreads) select_kernel(SelectArgs a) {
   const int64_t mat = (int64_t)b * a.G + g;
   const float* q = a.qp + mat * qb * P;
   const float* k = a.kp + mat * qb * P;
-  for (int e = threadIdx.x; e < ROWS * qstride; e += kScoreThreads) {
+  for (int e = threadIdx.x; e < ROWS * qstride; e += NT) {
     const int r = e / qstride;
     const int pcol = e % qstride;
     qs[e] = (r0 + r < a.q_end && pcol < P) ? q[(int64_t)(r0 + r) * P + pcol] : 0.0f;
   }
   // Only candidates j < q - local_window of the tile's last row are needed.
   const int ncols = max(0, min(qb, r0 + ROWS - a.local_window));
-  if constexpr (ROWS == 16 || ROWS == 8) {
+  if constexpr (ROWS == 16) {
+    // the host launches 16-row tiles only for P % 4 == 0 (select_rows_for)
+    __syncthreads();  // qs is complete before the first multiply
+    score_rows16_async(qs, qstride, k, P, ncols, kT, a.denom,
+                       [&](int r, int j, float s) { keys[r * qb + j] = order_key(s); });
+  } else if constexpr (ROWS == 8) {
     if (P % 4 == 0) {
       __syncthreads();  // qs is complete before the first multiply
       score_rows_async<ROWS / 4>(qs, qstride, k, P, ncols, kT, a.denom,
                                  [&](int r, int j, float s) { keys[r * qb + j] = order_key(s); });
-    } else if constexpr (ROWS == 16) {
-      for (int j0 = 0; j0 < ncols; j0 += kScoreThreads)
-        score_tile16(qs, qstride, k, P, j0, ncols, kT, a.denom,
-                     [&](int r, int j, float s) { keys[r * qb + j] = order_key(s); });
     } else {
       for (int j0 = 0; j0 < ncols; j0 += kScoreThreads)
         score_columns<ROWS>(qs, k, P, j0, ncols, kT, a.denom,
@@ -422,7 +522,7 @@ __global__ void __launch_bounds__(kScoreThreads) select_kernel(SelectArgs a) {
   __syncthreads();
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int r = warp; r < ROWS; r += kScoreThreads / 32) {
+  for (int r = warp; r < ROWS; r += NT / 32) {
     const int i = r0 + r;
     if (i >= a.q_end) break;
     const uint32_t* kr = keys + r * qb;
@@ -600,6 +700,124 @@ __global__ void validate_finish_kernel(unsigned long long* result) {
 }
 
 // ------------------------------------------------------------------ launchers
+// Projection with W held in shared memory.  The row-tiled project_kernel has
+// every CTA read the whole W from L2 in the same d order at the same time, so
+// the same few L2 lines serve every SM at once (32.6 us for 8192 rows x 128 x
+// 128 at config 2, ~4 us of fma work).  Here each of ~2 CTAs per SM copies W
+// into shared memory once, starting at a CTA-dependent 16-byte vector, then
+// projects its share of the rows 16 at a time: thread t owns column
+// p = t % P and rows t / P + i * (256 / P); x is read as broadcast float4s.
+// Each output is still one fma chain over d = 0..D-1 in order (bit-identical
+// to project_kernel / project_out_kernel).  Needs P | 256, P % 4 == 0,
+// D % 4 == 0 and a 16-byte aligned W.
+constexpr int kPwThreads = 256;
+constexpr int kPwRows = 16;
+
+template <typename T, int RPT>  // RPT = rows per thread = kPwRows * P / kPwThreads
+__global__ void __launch_bounds__(kPwThreads, 2) project_w_kernel(ProjRows j0, ProjRows j1, int ctas0, int D,
+                                                                   int P) {
+  extern __shared__ __align__(16) float pw_smem[];
+  float* Ws = pw_smem;         // [D][P]
+  float* xs = Ws + D * P;      // [kPwRows][D]
+  const bool second = static_cast<int>(blockIdx.x) >= ctas0;  // job fields are selected by value
+  const int cta = second ? blockIdx.x - ctas0 : blockIdx.x;
+  const int nct = second ? gridDim.x - ctas0 : ctas0;
+  const T* x = static_cast<const T*>(second ? j1.x : j0.x);
+  const float* W = second ? j1.W : j0.W;
+  float* out = second ? j1.out : j0.out;
+  const int qb = second ? j1.qb : j0.qb, row0 = second ? j1.row0 : j0.row0;
+  const int nrows = second ? j1.nrows : j0.nrows;
+  const int N = static_cast<int>((second ? j1.groups : j0.groups) * nrows);  // < 2^31 (host check)
+  const int lo = static_cast<int>((int64_t)N * cta / nct), hi = static_cast<int>((int64_t)N * (cta + 1) / nct);
+  if (lo >= hi) return;  // uniform per CTA
+  const int nv = D * P / 4;
+  const int start = static_cast<int>((int64_t)cta * 131 % nv);
+  for (int e = threadIdx.x; e < nv; e += kPwThreads) {
+    int v = e + start;
+    if (v >= nv) v -= nv;
+    cp_async16(Ws + 4 * v, W + 4 * (int64_t)v, 16);
+  }
+  cp_async_commit();
+  cp_async_wait<0>();
+  constexpr int H = kPwRows / RPT;  // row lanes: thread t takes rows t / P + i * H
+  const int p = threadIdx.x % P, h = threadIdx.x / P;
+  auto row_of = [&](int n) { return (int64_t)(n / nrows) * qb + row0 + n % nrows; };
+  for (int n0 = lo; n0 < hi; n0 += kPwRows) {
+    const int rows = min(kPwRows, hi - n0);
+    __syncthreads();  // W is in place; the previous rows are no longer read
+    for (int e = threadIdx.x; e < kPwRows * D; e += kPwThreads) {
+      const int r = e / D, d = e - r * D;
+      xs[e] = r < rows ? Elem<T>::to_f(x[row_of(n0 + r) * D + d]) : 0.0f;
+    }
+    __syncthreads();
+    float acc[RPT];
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) acc[i] = 0.0f;
+    for (int d = 0; d < D; d += 4) {
+      const float w0 = Ws[d * P + p], w1 = Ws[(d + 1) * P + p], w2 = Ws[(d + 2) * P + p], w3 = Ws[(d + 3) * P + p];
+      float4 xv[RPT];
+#pragma unroll
+      for (int i = 0; i < RPT; ++i) xv[i] = *reinterpret_cast<const float4*>(xs + (h + i * H) * D + d);
+#pragma unroll
+      for (int i = 0; i < RPT; ++i) acc[i] = __fmaf_rn(xv[i].x, w0, acc[i]);
+#pragma unroll
+      for (int i = 0; i < RPT; ++i) acc[i] = __fmaf_rn(xv[i].y, w1, acc[i]);
+#pragma unroll
+      for (int i = 0; i < RPT; ++i) acc[i] = __fmaf_rn(xv[i].z, w2, acc[i]);
+#pragma unroll
+      for (int i = 0; i < RPT; ++i) acc[i] = __fmaf_rn(xv[i].w, w3, acc[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) {
+      const int r = h + i * H;
+      if (r < rows) out[row_of(n0 + r) * P + p] = acc[i];
+    }
+  }
+}
+
+static bool project_w_fits(int D, int P, const float* W) {
+  return P >= 16 && P <= kPwThreads && kPwThreads % P == 0 && D % 4 == 0 &&
+         (size_t)(D * P + kPwRows * D) * sizeof(float) <= 96 * 1024 &&
+         (reinterpret_cast<uintptr_t>(W) & 15u) == 0;
+}
+
+template <typename T>
+cudaError_t launch_project_pair(const ProjRows& a, const ProjRows& b, int njobs, int D, int P, cudaStream_t stream) {
+  const int64_t na = a.groups * a.nrows, nb = njobs > 1 ? b.groups * b.nrows : 0;
+  const bool fits = project_w_fits(D, P, a.W) && (njobs < 2 || project_w_fits(D, P, b.W)) && na <= INT32_MAX &&
+                    nb <= INT32_MAX;
+  if (!fits || na + nb < 1024) {  // few rows: W copies would dominate; the per-row kernels instead
+    cudaError_t e = launch_project_rows<T>(a.x, a.groups, a.qb, a.row0, a.nrows, D, a.W, P, a.out, stream);
+    if (e == cudaSuccess && njobs > 1)
+      e = launch_project_rows<T>(b.x, b.groups, b.qb, b.row0, b.nrows, D, b.W, P, b.out, stream);
+    return e;
+  }
+  // ~2 CTAs per SM, split between the jobs by rows, at least one each, never more than their 16-row passes
+  const int64_t total = std::min<int64_t>(2 * 148, (na + nb + kPwRows - 1) / kPwRows);
+  int64_t ca = na == 0 ? 0 : std::max<int64_t>(1, total * na / (na + nb));
+  int64_t cb = nb == 0 ? 0 : std::max<int64_t>(1, total - ca);
+  ca = std::min<int64_t>(ca, (na + kPwRows - 1) / kPwRows);
+  cb = std::min<int64_t>(cb, (nb + kPwRows - 1) / kPwRows);
+  if (ca + cb == 0) return cudaSuccess;
+  const size_t smem = (size_t)(D * P + kPwRows * D) * sizeof(float);
+  auto go = [&](auto kernel) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    if (ca == 0)
+      kernel<<<(unsigned)cb, kPwThreads, smem, stream>>>(b, b, 0, D, P);
+    else
+      kernel<<<(unsigned)(ca + cb), kPwThreads, smem, stream>>>(a, b, (int)ca, D, P);
+    return cudaGetLastError();
+  };
+  switch (kPwRows * P / kPwThreads) {  // rows per thread
+    case 1: return go(project_w_kernel<T, 1>);
+    case 2: return go(project_w_kernel<T, 2>);
+    case 4: return go(project_w_kernel<T, 4>);
+    case 8: return go(project_w_kernel<T, 8>);
+    default: return go(project_w_kernel<T, 16>);
+  }
+}
+
 template <typename T>
 cudaError_t launch_project_rows(const void* x, int64_t groups, int qb, int row0, int nrows, int D, const float* W,
                                 int P, float* out, cudaStream_t stream) {
@@ -635,6 +853,10 @@ template cudaError_t launch_project_rows<__nv_bfloat16>(const void*, int64_t, in
                                                         float*, cudaStream_t);
 template cudaError_t launch_project_rows<__half>(const void*, int64_t, int, int, int, int, const float*, int, float*,
                                                  cudaStream_t);
+template cudaError_t launch_project_pair<float>(const ProjRows&, const ProjRows&, int, int, int, cudaStream_t);
+template cudaError_t launch_project_pair<__nv_bfloat16>(const ProjRows&, const ProjRows&, int, int, int,
+                                                        cudaStream_t);
+template cudaError_t launch_project_pair<__half>(const ProjRows&, const ProjRows&, int, int, int, cudaStream_t);
 template cudaError_t launch_project<float>(const void*, int64_t, int, const float*, int, float*, cudaStream_t);
 template cudaError_t launch_project<__nv_bfloat16>(const void*, int64_t, int, const float*, int, float*,
                                                    cudaStream_t);
@@ -655,8 +877,7 @@ cudaError_t launch_scores(const float* qp, const float* kp, int64_t R, int qb, i
 
 size_t select_smem_bytes(int rows, int qb, int P) {
   const int qstride = (P + 3) / 4 * 4 + 4;
-  const int stages = rows >= 8 ? 2 : 1;  // 8- and 16-row tiles double-buffer the key staging
-  return sizeof(float) * (rows * qstride + stages * kScoreThreads * kKStride) + sizeof(int) * 8 * 256 +
+  return sizeof(float) * (rows * qstride + select_stage_floats(rows)) +
          sizeof(uint32_t) * (size_t)rows * qb;
 }
 
@@ -667,16 +888,16 @@ static cudaError_t launch_select_rows(const SelectArgs& a, cudaStream_t stream) 
   if (e != cudaSuccess) return e;
   if (a.q_end <= a.q_begin) return cudaSuccess;
   dim3 grid((a.q_end - a.q_begin + ROWS - 1) / ROWS, a.G, a.B);
-  select_kernel<ROWS><<<grid, kScoreThreads, smem, stream>>>(a);
+  select_kernel<ROWS><<<grid, select_threads(ROWS), smem, stream>>>(a);
   return cudaGetLastError();
 }
 
-// Largest tile whose keys fit in shared memory; 16-row tiles only when they
+// Largest tile whose keys fit in shared memory; 16-row tiles (P % 4 == 0) only when they
 // still give two waves of CTAs (`tiles16` = CTAs at 16 rows, < 0 = unknown),
 // else 8-row tiles, which halve the rows per CTA and double the CTAs.
 int select_rows_for(int qb, int P, int64_t tiles16) {
   const size_t limit = 227 * 1024;
-  if (select_smem_bytes(16, qb, P) <= limit && (tiles16 < 0 || tiles16 >= 2 * 148)) return 16;
+  if (P % 4 == 0 && select_smem_bytes(16, qb, P) <= limit && (tiles16 < 0 || tiles16 >= 2 * 148)) return 16;
   if (select_smem_bytes(8, qb, P) <= limit) return 8;
   if (select_smem_bytes(4, qb, P) <= limit) return 4;
   return 0;
