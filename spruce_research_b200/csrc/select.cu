@@ -256,22 +256,32 @@ __device__ __forceinline__ void score_rows_async(const float* qs, int qstride, c
     const float* ks = ks2 + (st & 1) * (kScoreThreads * kKStride);
     const int pc = st % npc;
     const int p0 = pc * kPChunk;
-    const int pn = min(kPChunk, P - p0);
+    const int pn = P % kPChunk == 0 ? kPChunk : min(kPChunk, P - p0);
+#pragma unroll
     for (int pp = 0; pp < pn; pp += 4) {
       float4 qv[RM], kv[4];
 #pragma unroll
       for (int r = 0; r < RM; ++r) qv[r] = *reinterpret_cast<const float4*>(qs + (RM * rg + r) * qstride + p0 + pp);
 #pragma unroll
       for (int c = 0; c < 4; ++c) kv[c] = *reinterpret_cast<const float4*>(ks + (cg + 64 * c) * kKStride + pp);
+      // p = pp, pp+1, pp+2, pp+3 in turn across all RM x 4 accumulators: each chain keeps its order,
+      // and consecutive fmas are independent (no wait on the previous one's result)
 #pragma unroll
       for (int r = 0; r < RM; ++r)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          acc[r][c] = __fmaf_rn(qv[r].x, kv[c].x, acc[r][c]);
-          acc[r][c] = __fmaf_rn(qv[r].y, kv[c].y, acc[r][c]);
-          acc[r][c] = __fmaf_rn(qv[r].z, kv[c].z, acc[r][c]);
-          acc[r][c] = __fmaf_rn(qv[r].w, kv[c].w, acc[r][c]);
-        }
+        for (int c = 0; c < 4; ++c) acc[r][c] = __fmaf_rn(qv[r].x, kv[c].x, acc[r][c]);
+#pragma unroll
+      for (int r = 0; r < RM; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[r][c] = __fmaf_rn(qv[r].y, kv[c].y, acc[r][c]);
+#pragma unroll
+      for (int r = 0; r < RM; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[r][c] = __fmaf_rn(qv[r].z, kv[c].z, acc[r][c]);
+#pragma unroll
+      for (int r = 0; r < RM; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[r][c] = __fmaf_rn(qv[r].w, kv[c].w, acc[r][c]);
     }
     if (pc == npc - 1) {
       const int j0 = (st / npc) * kScoreThreads;
@@ -344,21 +354,35 @@ __device__ __forceinline__ void score_rows16_async(const float* qs, int qstride,
     const float* ks = ks2 + (st & 1) * (kSlab16 * kK16Stride);
     const int pc = st % npc;
     const int p0 = pc * kP16;
-    const int pn = min(kP16, P - p0);
+    const int pn = P % kP16 == 0 ? kP16 : min(kP16, P - p0);
+#pragma unroll
     for (int pp = 0; pp < pn; pp += 4) {
       const float4 k0 = *reinterpret_cast<const float4*>(ks + ct * kK16Stride + pp);
       const float4 k1 = *reinterpret_cast<const float4*>(ks + (ct + 256) * kK16Stride + pp);
+      float4 qv[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) qv[r] = *reinterpret_cast<const float4*>(qrow + r * qstride + p0 + pp);
+      // p = pp .. pp+3 in turn across all 16 accumulators: each chain keeps its order, and
+      // consecutive fmas are independent
 #pragma unroll
       for (int r = 0; r < 8; ++r) {
-        const float4 qv = *reinterpret_cast<const float4*>(qrow + r * qstride + p0 + pp);
-        acc[r][0] = __fmaf_rn(qv.x, k0.x, acc[r][0]);
-        acc[r][1] = __fmaf_rn(qv.x, k1.x, acc[r][1]);
-        acc[r][0] = __fmaf_rn(qv.y, k0.y, acc[r][0]);
-        acc[r][1] = __fmaf_rn(qv.y, k1.y, acc[r][1]);
-        acc[r][0] = __fmaf_rn(qv.z, k0.z, acc[r][0]);
-        acc[r][1] = __fmaf_rn(qv.z, k1.z, acc[r][1]);
-        acc[r][0] = __fmaf_rn(qv.w, k0.w, acc[r][0]);
-        acc[r][1] = __fmaf_rn(qv.w, k1.w, acc[r][1]);
+        acc[r][0] = __fmaf_rn(qv[r].x, k0.x, acc[r][0]);
+        acc[r][1] = __fmaf_rn(qv[r].x, k1.x, acc[r][1]);
+      }
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        acc[r][0] = __fmaf_rn(qv[r].y, k0.y, acc[r][0]);
+        acc[r][1] = __fmaf_rn(qv[r].y, k1.y, acc[r][1]);
+      }
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        acc[r][0] = __fmaf_rn(qv[r].z, k0.z, acc[r][0]);
+        acc[r][1] = __fmaf_rn(qv[r].z, k1.z, acc[r][1]);
+      }
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        acc[r][0] = __fmaf_rn(qv[r].w, k0.w, acc[r][0]);
+        acc[r][1] = __fmaf_rn(qv[r].w, k1.w, acc[r][1]);
       }
     }
     if (pc == npc - 1) {
@@ -473,11 +497,13 @@ __device__ __forceinline__ uint32_t warp_radix_select(const uint32_t* keys, int 
   return prefix;
 }
 
-template <int ROWS>
+// PFIX > 0: the projection width is PFIX at compile time (strides and the
+// p loops fold to constants); PFIX = 0: a.P at run time.
+template <int ROWS, int PFIX>
 __global__ void __launch_bounds__(select_threads(ROWS), ROWS >= 16 ? 1 : 2) select_kernel(SelectArgs a) {
   constexpr int NT = select_threads(ROWS);
   extern __shared__ float sm[];
-  const int P = a.P;
+  const int P = PFIX > 0 ? PFIX : a.P;
   const int qb = a.qb;
   const int qstride = (P + 3) / 4 * 4 + 4;           // padded row stride of qs (16-byte aligned rows)
   float* qs = sm;                                   // [ROWS][qstride]
@@ -884,11 +910,12 @@ size_t select_smem_bytes(int rows, int qb, int P) {
 template <int ROWS>
 static cudaError_t launch_select_rows(const SelectArgs& a, cudaStream_t stream) {
   const size_t smem = select_smem_bytes(ROWS, a.qb, a.P);
-  cudaError_t e = cudaFuncSetAttribute(select_kernel<ROWS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  auto kernel = a.P == 128 ? select_kernel<ROWS, 128> : select_kernel<ROWS, 0>;  // 128: the gate width in use
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   if (a.q_end <= a.q_begin) return cudaSuccess;
   dim3 grid((a.q_end - a.q_begin + ROWS - 1) / ROWS, a.G, a.B);
-  select_kernel<ROWS><<<grid, select_threads(ROWS), smem, stream>>>(a);
+  kernel<<<grid, select_threads(ROWS), smem, stream>>>(a);
   return cudaGetLastError();
 }
 
