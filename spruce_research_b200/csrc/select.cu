@@ -355,34 +355,56 @@ __device__ __forceinline__ void score_rows16_async(const float* qs, int qstride,
     const int pc = st % npc;
     const int p0 = pc * kP16;
     const int pn = P % kP16 == 0 ? kP16 : min(kP16, P - p0);
+    // Columns past the tile's causal range are not multiplied: a warp skips each
+    // of its two 32-column sets that lies wholly at or past ncols (warp-uniform).
+    const int jw = (st / npc) * kSlab16 + (ct & ~31);
+    const bool c0 = jw < ncols, c1 = jw + 256 < ncols;
+    if (c1) {
 #pragma unroll
-    for (int pp = 0; pp < pn; pp += 4) {
-      const float4 k0 = *reinterpret_cast<const float4*>(ks + ct * kK16Stride + pp);
-      const float4 k1 = *reinterpret_cast<const float4*>(ks + (ct + 256) * kK16Stride + pp);
-      float4 qv[8];
+      for (int pp = 0; pp < pn; pp += 4) {
+        const float4 k0 = *reinterpret_cast<const float4*>(ks + ct * kK16Stride + pp);
+        const float4 k1 = *reinterpret_cast<const float4*>(ks + (ct + 256) * kK16Stride + pp);
+        float4 qv[8];
 #pragma unroll
-      for (int r = 0; r < 8; ++r) qv[r] = *reinterpret_cast<const float4*>(qrow + r * qstride + p0 + pp);
-      // p = pp .. pp+3 in turn across all 16 accumulators: each chain keeps its order, and
-      // consecutive fmas are independent
+        for (int r = 0; r < 8; ++r) qv[r] = *reinterpret_cast<const float4*>(qrow + r * qstride + p0 + pp);
+        // p = pp .. pp+3 in turn across all 16 accumulators: each chain keeps its order, and
+        // consecutive fmas are independent
 #pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        acc[r][0] = __fmaf_rn(qv[r].x, k0.x, acc[r][0]);
-        acc[r][1] = __fmaf_rn(qv[r].x, k1.x, acc[r][1]);
+        for (int r = 0; r < 8; ++r) {
+          acc[r][0] = __fmaf_rn(qv[r].x, k0.x, acc[r][0]);
+          acc[r][1] = __fmaf_rn(qv[r].x, k1.x, acc[r][1]);
+        }
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          acc[r][0] = __fmaf_rn(qv[r].y, k0.y, acc[r][0]);
+          acc[r][1] = __fmaf_rn(qv[r].y, k1.y, acc[r][1]);
+        }
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          acc[r][0] = __fmaf_rn(qv[r].z, k0.z, acc[r][0]);
+          acc[r][1] = __fmaf_rn(qv[r].z, k1.z, acc[r][1]);
+        }
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          acc[r][0] = __fmaf_rn(qv[r].w, k0.w, acc[r][0]);
+          acc[r][1] = __fmaf_rn(qv[r].w, k1.w, acc[r][1]);
+        }
       }
+    } else if (c0) {
 #pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        acc[r][0] = __fmaf_rn(qv[r].y, k0.y, acc[r][0]);
-        acc[r][1] = __fmaf_rn(qv[r].y, k1.y, acc[r][1]);
-      }
+      for (int pp = 0; pp < pn; pp += 4) {
+        const float4 k0 = *reinterpret_cast<const float4*>(ks + ct * kK16Stride + pp);
+        float4 qv[8];
 #pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        acc[r][0] = __fmaf_rn(qv[r].z, k0.z, acc[r][0]);
-        acc[r][1] = __fmaf_rn(qv[r].z, k1.z, acc[r][1]);
-      }
+        for (int r = 0; r < 8; ++r) qv[r] = *reinterpret_cast<const float4*>(qrow + r * qstride + p0 + pp);
 #pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        acc[r][0] = __fmaf_rn(qv[r].w, k0.w, acc[r][0]);
-        acc[r][1] = __fmaf_rn(qv[r].w, k1.w, acc[r][1]);
+        for (int r = 0; r < 8; ++r) acc[r][0] = __fmaf_rn(qv[r].x, k0.x, acc[r][0]);
+#pragma unroll
+        for (int r = 0; r < 8; ++r) acc[r][0] = __fmaf_rn(qv[r].y, k0.y, acc[r][0]);
+#pragma unroll
+        for (int r = 0; r < 8; ++r) acc[r][0] = __fmaf_rn(qv[r].z, k0.z, acc[r][0]);
+#pragma unroll
+        for (int r = 0; r < 8; ++r) acc[r][0] = __fmaf_rn(qv[r].w, k0.w, acc[r][0]);
       }
     }
     if (pc == npc - 1) {
