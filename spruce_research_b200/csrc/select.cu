@@ -475,15 +475,21 @@ struct SelectArgs {
 // Radix select of the k-th largest key among keys[lo, hi) (k >= 1, k <= hi-lo)
 // by one warp.  Returns the threshold key; *need = how many keys equal to the
 // threshold belong to the top k (taken lowest index first).
+// After each of the first three 8-bit passes the keys that share the new
+// prefix (their number is the chosen digit's count) are copied into the warp's
+// list cbuf (capacity ccap) when they fit, and the next pass reads only that
+// list; the threshold and *need do not depend on the keys' order.
 __device__ __forceinline__ uint32_t warp_radix_select(const uint32_t* keys, int lo, int hi, int k, int* hist,
-                                                      int* need) {
+                                                      uint32_t* cbuf, int ccap, int* need) {
   const int lane = threadIdx.x & 31;
   uint32_t prefix = 0, pmask = 0;
+  const uint32_t* src = keys + lo;  // the keys a pass reads: src[0, n)
+  int n = hi - lo;
   for (int shift = 24; shift >= 0; shift -= 8) {
     for (int b = lane; b < 256; b += 32) hist[b] = 0;
     __syncwarp();
-    for (int j = lo + lane; j < hi; j += 32) {
-      const uint32_t key = keys[j];
+    for (int j = lane; j < n; j += 32) {
+      const uint32_t key = src[j];
       if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1);
     }
     __syncwarp();
@@ -510,10 +516,28 @@ __device__ __forceinline__ uint32_t warp_radix_select(const uint32_t* keys, int 
     }
     digit = __shfl_sync(0xffffffffu, digit, hl);
     above = __shfl_sync(0xffffffffu, above, hl);
+    const int cnt = hist[digit];  // keys sharing the new prefix
     prefix |= static_cast<uint32_t>(digit) << shift;
     pmask |= 0xFFu << shift;
     k -= above;
     __syncwarp();
+    if (shift > 0 && cnt <= ccap && cnt < n) {
+      // In place when src is already cbuf: a chunk's keys are all read before any
+      // of them is written, and a key is written at or below its read position.
+      int pos = 0;
+      for (int j0 = 0; j0 < n; j0 += 32) {
+        const int j = j0 + lane;
+        const uint32_t key = j < n ? src[j] : 0u;
+        const bool keep = j < n && (key & pmask) == prefix;
+        const unsigned bm = __ballot_sync(0xffffffffu, keep);
+        __syncwarp();
+        if (keep) cbuf[pos + __popc(bm & ((1u << lane) - 1u))] = key;
+        pos += __popc(bm);
+      }
+      __syncwarp();
+      src = cbuf;
+      n = pos;
+    }
   }
   *need = k;
   return prefix;
@@ -570,6 +594,9 @@ __global__ void __launch_bounds__(select_threads(ROWS), ROWS >= 16 ? 1 : 2) sele
   __syncthreads();
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // the rest of the staging: one list of keys per warp for the radix select
+  constexpr int ccap = (select_stage_floats(ROWS) - NT / 32 * 256) / (NT / 32);
+  uint32_t* cbuf = reinterpret_cast<uint32_t*>(hist + NT / 32 * 256);
   for (int r = warp; r < ROWS; r += NT / 32) {
     const int i = r0 + r;
     if (i >= a.q_end) break;
@@ -580,7 +607,8 @@ __global__ void __launch_bounds__(select_threads(ROWS), ROWS >= 16 ? 1 : 2) sele
     uint32_t thr = 0;
     int need = 0;
     const bool partial = n > a.W;  // more candidates than free slots: top-W only
-    if (partial && a.W > 0) thr = warp_radix_select(kr, lo, hi, a.W, hist + warp * 256, &need);
+    if (partial && a.W > 0)
+      thr = warp_radix_select(kr, lo, hi, a.W, hist + warp * 256, cbuf + warp * ccap, ccap, &need);
     int32_t* o = a.out + b * a.osb + g * a.osg + (int64_t)i * a.osq;
     int pos = 0, ties = 0;
     for (int j0 = 0; j0 <= i; j0 += 32) {
