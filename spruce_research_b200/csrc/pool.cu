@@ -12,8 +12,9 @@
 // (coalesced along D) and each 64-token block writes one pooled row (P = 1).
 // At config 2 that is Q (0.94 GB) and K (0.13 GB) read once and 8.4 MB written:
 // an HBM-bound job.  P = 1 runs pool_rows_kernel (one thread per 16-row chunk
-// and 16-byte vector, sums in registers); prototypes (P > 1) need every row of
-// the block at once and run pool_block_kernel (rows staged in shared memory).
+// and 16-byte vector, loads staged by cp.async, sums in registers); prototypes
+// (P > 1) need every row of the block at once and run pool_block_kernel (rows
+// staged in shared memory).
 #include <algorithm>
 
 #include "common.cuh"
@@ -275,6 +276,72 @@ __device__ __forceinline__ void chunk_sum(const T* p, int64_t sh, int64_t st, in
   }
 }
 
+// The same in-order chunk sum with the rows' loads staged in shared memory by
+// cp.async: the data in flight costs no registers, so a thread keeps
+// kStageVecs / REP rows (14-16 16-byte vectors) in flight where the register
+// form held one row.  stage[v * stride] is the thread's vector v.  A row's
+// slot is refilled only after its values were added (the adds use the data, so
+// the slot's shared loads have completed).
+constexpr int kStageVecs = 16;
+
+__device__ __forceinline__ void pool_cp16(uint4* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void pool_cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void pool_cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+template <typename T, int REP>
+__device__ __forceinline__ void chunk_sum_staged(const T* p, int64_t sh, int64_t st, int nrows, uint4* stage,
+                                                 int stride, float (&s)[Vec16<T>::N]) {
+  constexpr int VN = Vec16<T>::N;
+  constexpr int S = kStageVecs / REP;  // rows in flight
+  static_assert(S >= 1, "a row must fit in the stage");
+  auto issue = [&](int r) {  // one commit group per row, empty past the real rows
+    if (r < nrows) {
+#pragma unroll
+      for (int h = 0; h < REP; ++h) pool_cp16(stage + ((r % S) * REP + h) * stride, p + r * st + h * sh);
+    }
+    pool_cp_commit();
+  };
+#pragma unroll
+  for (int r = 0; r < S; ++r) issue(r);
+#pragma unroll 1
+  for (int r = 0; r < 16; ++r) {
+    pool_cp_wait<S - 1>();  // row r has landed
+    float g[VN];
+    if (r < nrows) {
+      float acc[VN];
+#pragma unroll
+      for (int k = 0; k < VN; ++k) acc[k] = 0.0f;
+#pragma unroll
+      for (int h = 0; h < REP; ++h) {
+        const uint4 raw = stage[((r % S) * REP + h) * stride];
+        const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+        for (int k = 0; k < VN; ++k) acc[k] = __fadd_rn(acc[k], Elem<T>::to_f(e[k]));
+      }
+      if constexpr (REP == 1) {
+#pragma unroll
+        for (int k = 0; k < VN; ++k) g[k] = acc[k];  // 0 + x: the reference's -0 -> +0 is kept
+      } else if constexpr ((REP & (REP - 1)) == 0) {
+#pragma unroll
+        for (int k = 0; k < VN; ++k) g[k] = round_through<T>(__fmul_rn(acc[k], 1.0f / REP));
+      } else {
+#pragma unroll
+        for (int k = 0; k < VN; ++k) g[k] = round_through<T>(__fdiv_rn(acc[k], static_cast<float>(REP)));
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < VN; ++k) g[k] = 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < VN; ++k) s[k] = __fadd_rn(s[k], g[k]);
+    issue(r + S);
+  }
+  pool_cp_wait<0>();
+}
+
 // items = (batch, block, slot) with the slots of one block adjacent (slot s <
 // j0.hout is job 0's head s, the rest job 1's); each CTA takes `ipc` items of
 // 4 * (D / VN) threads.
@@ -284,6 +351,7 @@ __global__ void __launch_bounds__(kRowsThreads, 3) pool_rows_kernel(PoolJob j0, 
                                                                   int ipc) {
   constexpr int VN = Vec16<T>::N;
   __shared__ __align__(16) float part[kRowsThreads * VN];
+  extern __shared__ __align__(16) uint4 pool_stage[];  // [kStageVecs][blockDim.x]
   const int nvec = D / VN;
   const int per_item = 4 * nvec;
   const int t = threadIdx.x;
@@ -316,12 +384,14 @@ __global__ void __launch_bounds__(kRowsThreads, 3) pool_rows_kernel(PoolJob j0, 
       const int nrows = max(0, min(16, count - 16 * c));
       const T* p = static_cast<const T*>(second ? j1.x : j0.x) + b * (second ? j1.sb : j0.sb) +
                    (int64_t)(y * rep) * sh + (int64_t)(t0 + 16 * c) * st + v * VN;
+      uint4* stage = pool_stage + t;
+      const int stride = blockDim.x;
       switch (rep) {
-        case 1: chunk_sum<T, 1>(p, sh, st, nrows, rep, s); break;
-        case 2: chunk_sum<T, 2>(p, sh, st, nrows, rep, s); break;
-        case 4: chunk_sum<T, 4>(p, sh, st, nrows, rep, s); break;
-        case 7: chunk_sum<T, 7>(p, sh, st, nrows, rep, s); break;
-        case 8: chunk_sum<T, 8>(p, sh, st, nrows, rep, s); break;
+        case 1: chunk_sum_staged<T, 1>(p, sh, st, nrows, stage, stride, s); break;
+        case 2: chunk_sum_staged<T, 2>(p, sh, st, nrows, stage, stride, s); break;
+        case 4: chunk_sum_staged<T, 4>(p, sh, st, nrows, stage, stride, s); break;
+        case 7: chunk_sum_staged<T, 7>(p, sh, st, nrows, stage, stride, s); break;
+        case 8: chunk_sum_staged<T, 8>(p, sh, st, nrows, stage, stride, s); break;
         default: chunk_sum<T, 0>(p, sh, st, nrows, rep, s); break;
       }
     }
@@ -362,8 +432,12 @@ cudaError_t launch_pool(PoolJob j0, PoolJob j1, int njobs, int B, int T_len, int
     const int64_t items = (int64_t)B * gx * slots;
     const int64_t ctas = (items + ipc - 1) / ipc;
     if (ctas > INT32_MAX) return cudaErrorInvalidValue;
-    pool_rows_kernel<T><<<(unsigned)ctas, ipc * per_item, 0, stream>>>(j0, j1, njobs, T_len, D, nb, gx, slots,
-                                                                        items, ipc);
+    const size_t stage = sizeof(uint4) * kStageVecs * ipc * per_item;
+    cudaError_t e = cudaFuncSetAttribute(pool_rows_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)stage);
+    if (e != cudaSuccess) return e;
+    pool_rows_kernel<T><<<(unsigned)ctas, ipc * per_item, stage, stream>>>(j0, j1, njobs, T_len, D, nb, gx,
+                                                                            slots, items, ipc);
     return cudaGetLastError();
   }
   dim3 grid(gx, slots, B);
