@@ -524,7 +524,7 @@ def run_b200(args):
                      "peak_source": peak_src + ", of measured",
                      "frac_of_sustained": achieved / measured_peak(sustained=True)[0],
                      "flops_per_launch": r_flops, "traffic": profiled_traffic(shape.tokens)},
-        "gpu_launches": SparsePrefillLayer.LAUNCHES_PER_CALL * args.steps,
+        "gpu_launches": layer.launches_per_call(B, g1 - g0, (i0, i1)) * args.steps,
         "clocks": clocks.summary(),
         "parity": parity,
     }

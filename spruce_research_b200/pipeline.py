@@ -2,8 +2,9 @@
 
 This is the per-layer hot path the benchmarks time: pooled Q/K features,
 FlatGate scores, masked top-k packed into ``selected_blocks`` rows, and causal
-GQA block-sparse attention over those rows -- five kernel launches, no host
-synchronisation, buffers reused across calls.
+GQA block-sparse attention over those rows -- four kernel launches (five when
+the projections run separately), no host synchronisation, buffers reused
+across calls.
 
 Reference composition: teacher/chunked_extract.py:164-172 (feature capture),
 selector/gate.py:80-101 (scores), scripts/route_overrides.py:187-205 and
@@ -28,9 +29,6 @@ class SparsePrefillLayer:
     Calls return ``(out [B, T, Hq, D], selected [B, Hkv, qb, K] int32)``.
     """
 
-    #: kernels launched per call (pool, 2 projections, select, attention)
-    LAUNCHES_PER_CALL = 5
-
     def __init__(self, wq: torch.Tensor, wk: torch.Tensor, k_selected: int, local_window: int = 0,
                  sink_blocks: int = 1):
         self.wq = wq.detach().float().contiguous()
@@ -39,6 +37,20 @@ class SparsePrefillLayer:
         self.local_window = int(local_window)
         self.sink_blocks = int(sink_blocks)
         self._workspace = None
+
+    def launches_per_call(self, batch: int, groups: int, q_blocks: tuple[int, int]) -> int:
+        """Kernels one call launches: pool, the projections, select, attention.
+
+        Both projections share one launch (W in shared memory) when the call
+        projects at least 1024 rows and W fits that kernel; otherwise each has
+        its own (the rule of ``launch_project_pair`` in ``csrc/select.cu``).
+        """
+        d, p = self.wq.shape
+        i0, i1 = q_blocks
+        rows = batch * groups * ((i1 - i0) + max(1, i1))
+        fused = (16 <= p <= 256 and 256 % p == 0 and d % 4 == 0 and (d * p + 16 * d) * 4 <= 96 * 1024
+                 and rows >= 1024)
+        return 4 if fused else 5
 
     def select(self, q: torch.Tensor, k: torch.Tensor, out: torch.Tensor | None = None,
                q_blocks: tuple[int, int] | None = None) -> torch.Tensor:
