@@ -794,7 +794,8 @@ __global__ void __launch_bounds__(kPwThreads, 2) project_w_kernel(ProjRows j0, P
                                                                    int P) {
   extern __shared__ __align__(16) float pw_smem[];
   float* Ws = pw_smem;         // [D][P]
-  float* xs = Ws + D * P;      // [kPwRows][D]
+  float* xs = Ws + D * P;      // [kPwRows][D] this pass's rows in fp32
+  T* raw = reinterpret_cast<T*>(xs + kPwRows * D);  // [2][kPwRows][D] rows as loaded, two passes
   const bool second = static_cast<int>(blockIdx.x) >= ctas0;  // job fields are selected by value
   const int cta = second ? blockIdx.x - ctas0 : blockIdx.x;
   const int nct = second ? gridDim.x - ctas0 : ctas0;
@@ -814,16 +815,40 @@ __global__ void __launch_bounds__(kPwThreads, 2) project_w_kernel(ProjRows j0, P
     cp_async16(Ws + 4 * v, W + 4 * (int64_t)v, 16);
   }
   cp_async_commit();
-  cp_async_wait<0>();
   constexpr int H = kPwRows / RPT;  // row lanes: thread t takes rows t / P + i * H
+  constexpr int VE = 16 / static_cast<int>(sizeof(T));  // elements per 16-byte chunk
   const int p = threadIdx.x % P, h = threadIdx.x / P;
+  const int cpr = D / VE;  // chunks per row
   auto row_of = [&](int n) { return (int64_t)(n / nrows) * qb + row0 + n % nrows; };
-  for (int n0 = lo; n0 < hi; n0 += kPwRows) {
+  // The next pass's rows are fetched by cp.async while this pass multiplies
+  // (rows past the CTA's share are zero-filled).
+  auto fetch = [&](int n0, int buf) {
     const int rows = min(kPwRows, hi - n0);
-    __syncthreads();  // W is in place; the previous rows are no longer read
-    for (int e = threadIdx.x; e < kPwRows * D; e += kPwThreads) {
-      const int r = e / D, d = e - r * D;
-      xs[e] = r < rows ? Elem<T>::to_f(x[row_of(n0 + r) * D + d]) : 0.0f;
+    T* dst = raw + buf * kPwRows * D;
+    for (int c = threadIdx.x; c < kPwRows * cpr; c += kPwThreads) {
+      const int r = c / cpr, k = c - r * cpr;
+      const bool ok = r < rows;
+      const T* src = ok ? x + row_of(n0 + r) * D + k * VE : x;
+      cp_async16(reinterpret_cast<float*>(dst + c * VE), reinterpret_cast<const float*>(src), ok ? 16 : 0);
+    }
+    cp_async_commit();
+  };
+  fetch(lo, 0);
+  int buf = 0;
+  for (int n0 = lo; n0 < hi; n0 += kPwRows, buf ^= 1) {
+    const int rows = min(kPwRows, hi - n0);
+    if (n0 + kPwRows < hi) {
+      fetch(n0 + kPwRows, buf ^ 1);
+      cp_async_wait<1>();  // W and this pass's rows have landed
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();  // ... for every thread, and the previous pass no longer reads xs
+    for (int c = threadIdx.x; c < kPwRows * cpr; c += kPwThreads) {
+      const uint4 v = *reinterpret_cast<const uint4*>(raw + buf * kPwRows * D + c * VE);
+      const T* e = reinterpret_cast<const T*>(&v);
+#pragma unroll
+      for (int k = 0; k < VE; ++k) xs[c * VE + k] = Elem<T>::to_f(e[k]);
     }
     __syncthreads();
     float acc[RPT];
@@ -851,23 +876,43 @@ __global__ void __launch_bounds__(kPwThreads, 2) project_w_kernel(ProjRows j0, P
   }
 }
 
+// Shared memory of project_w_kernel: W, the fp32 rows, two passes of rows as loaded.
+static size_t project_w_smem(int D, int P, size_t elem) {
+  return (size_t)(D * P + kPwRows * D) * sizeof(float) + 2 * (size_t)kPwRows * D * elem;
+}
+
 static bool project_w_fits(int D, int P, const float* W) {
-  return P >= 16 && P <= kPwThreads && kPwThreads % P == 0 && D % 4 == 0 &&
-         (size_t)(D * P + kPwRows * D) * sizeof(float) <= 96 * 1024 &&
+  return P >= 16 && P <= kPwThreads && kPwThreads % P == 0 && D % 4 == 0 && (D * 2) % 16 == 0 &&
+         project_w_smem(D, P, sizeof(float)) <= 96 * 1024 &&
          (reinterpret_cast<uintptr_t>(W) & 15u) == 0;
 }
+
+// project_w_kernel takes the jobs: at least 1024 rows in all (fewer, and the W
+// copies would dominate), and W, P and D within its limits.
+static bool project_w_takes(int64_t na, int64_t nb, int D, int P, const float* Wa, const float* Wb) {
+  return na + nb >= 1024 && na <= INT32_MAX && nb <= INT32_MAX && project_w_fits(D, P, Wa) &&
+         (Wb == nullptr || project_w_fits(D, P, Wb));
+}
+
+template <typename T>
+static cudaError_t launch_project_w(const ProjRows& a, const ProjRows& b, int njobs, int D, int P,
+                                    cudaStream_t stream);
 
 template <typename T>
 cudaError_t launch_project_pair(const ProjRows& a, const ProjRows& b, int njobs, int D, int P, cudaStream_t stream) {
   const int64_t na = a.groups * a.nrows, nb = njobs > 1 ? b.groups * b.nrows : 0;
-  const bool fits = project_w_fits(D, P, a.W) && (njobs < 2 || project_w_fits(D, P, b.W)) && na <= INT32_MAX &&
-                    nb <= INT32_MAX;
-  if (!fits || na + nb < 1024) {  // few rows: W copies would dominate; the per-row kernels instead
-    cudaError_t e = launch_project_rows<T>(a.x, a.groups, a.qb, a.row0, a.nrows, D, a.W, P, a.out, stream);
-    if (e == cudaSuccess && njobs > 1)
-      e = launch_project_rows<T>(b.x, b.groups, b.qb, b.row0, b.nrows, D, b.W, P, b.out, stream);
-    return e;
-  }
+  if (project_w_takes(na, nb, D, P, a.W, njobs > 1 ? b.W : nullptr))
+    return launch_project_w<T>(a, b, njobs, D, P, stream);
+  cudaError_t e = launch_project_rows<T>(a.x, a.groups, a.qb, a.row0, a.nrows, D, a.W, P, a.out, stream);
+  if (e == cudaSuccess && njobs > 1)
+    e = launch_project_rows<T>(b.x, b.groups, b.qb, b.row0, b.nrows, D, b.W, P, b.out, stream);
+  return e;
+}
+
+template <typename T>
+static cudaError_t launch_project_w(const ProjRows& a, const ProjRows& b, int njobs, int D, int P,
+                                    cudaStream_t stream) {
+  const int64_t na = a.groups * a.nrows, nb = njobs > 1 ? b.groups * b.nrows : 0;
   // ~2 CTAs per SM, split between the jobs by rows, at least one each, never more than their 16-row passes
   const int64_t total = std::min<int64_t>(2 * 148, (na + nb + kPwRows - 1) / kPwRows);
   int64_t ca = na == 0 ? 0 : std::max<int64_t>(1, total * na / (na + nb));
@@ -875,7 +920,8 @@ cudaError_t launch_project_pair(const ProjRows& a, const ProjRows& b, int njobs,
   ca = std::min<int64_t>(ca, (na + kPwRows - 1) / kPwRows);
   cb = std::min<int64_t>(cb, (nb + kPwRows - 1) / kPwRows);
   if (ca + cb == 0) return cudaSuccess;
-  const size_t smem = (size_t)(D * P + kPwRows * D) * sizeof(float);
+  if ((D * sizeof(T)) % 16 != 0) return cudaErrorInvalidValue;  // callers pass 16-byte rows
+  const size_t smem = project_w_smem(D, P, sizeof(T));
   auto go = [&](auto kernel) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
@@ -899,6 +945,10 @@ cudaError_t launch_project_rows(const void* x, int64_t groups, int qb, int row0,
                                 int P, float* out, cudaStream_t stream) {
   const int64_t N = groups * nrows;
   if (N == 0) return cudaSuccess;
+  if (project_w_takes(N, 0, D, P, W, nullptr)) {
+    const ProjRows job{x, W, out, groups, qb, row0, nrows};
+    return launch_project_w<T>(job, job, 1, D, P, stream);
+  }
   if (N * P <= (int64_t)148 * 128 * 16) {  // fewer outputs than 16 per-output threads per SM-lane
     project_out_kernel<T><<<(unsigned)((N * P + 127) / 128), 128, 0, stream>>>(static_cast<const T*>(x), N, D, W, P,
                                                                               out, qb, row0, nrows);
