@@ -83,6 +83,8 @@ def parse_args():
     ap.add_argument("--e2e-chunks", type=int, default=16, help="query-block chunks of the streamed e2e step")
     ap.add_argument("--e2e-schedule", choices=("balanced", "equal"), default="balanced",
                     help="chunk bounds of the streamed e2e step: equal attention work or equal query blocks")
+    ap.add_argument("--no-numa-bind", action="store_true",
+                    help="pin the e2e host buffers wherever the process runs, not on the GPU's NUMA node")
     ap.add_argument("--cpu-seconds", type=float, default=24.0, help="target length of one CPU sample")
     ap.add_argument("--gather", choices=("fused", "nccl"), default="fused",
                     help="N>1 output all-gather: NVLink peer stores in the attention epilogue, or NCCL")
@@ -318,7 +320,7 @@ def run_b200(args):
     import torch
     import torch.distributed as dist
 
-    from spruce_research_b200 import native
+    from spruce_research_b200 import hostmem, native
     from spruce_research_b200.pipeline import HostStreamedLayer, SparsePrefillLayer
     from spruce_research_b200.sharding import PeerOutput, ShardedSparsePrefill, plan
     from spruce_research_b200.synthetic import make_gate_weights, make_layer_inputs
@@ -421,12 +423,16 @@ def run_b200(args):
     # ---- end to end through the public API with pinned host buffers
     e2e = None
     if not args.no_e2e:
-        hq = q[:, g0 * rep:g1 * rep].transpose(1, 2).contiguous().cpu().pin_memory()   # [B, T, Hr, D]
-        hk = k[:, g0:g1].transpose(1, 2).contiguous().cpu().pin_memory()
-        hv = v[:, g0:g1].transpose(1, 2).contiguous().cpu().pin_memory()
+        # pinned on this GPU's NUMA node (hostmem.near), unless --no-numa-bind
+        pin = (lambda t: t.contiguous().cpu().pin_memory()) if args.no_numa_bind else \
+            (lambda t: hostmem.pinned_copy(t, dev))
+        hq = pin(q[:, g0 * rep:g1 * rep].transpose(1, 2))   # [B, T, Hr, D]
+        hk = pin(k[:, g0:g1].transpose(1, 2))
+        hv = pin(v[:, g0:g1].transpose(1, 2))
         dq, dk, dv = (torch.empty_like(t, device=dev) for t in (hq, hk, hv))
         # each rank reads back the rows and heads it computed: over all ranks, the whole output
-        hout = torch.empty((B, T, (g1 - g0) * rep, D), dtype=torch.bfloat16).pin_memory()
+        hout = (torch.empty((B, T, (g1 - g0) * rep, D), dtype=torch.bfloat16).pin_memory() if args.no_numa_bind
+                else hostmem.pinned_empty((B, T, (g1 - g0) * rep, D), torch.bfloat16, dev))
         streamer = HostStreamedLayer(layer, dev, chunks=args.e2e_chunks, schedule=args.e2e_schedule)
 
         def e2e_step():
@@ -458,7 +464,9 @@ def run_b200(args):
                         f"{args.e2e_schedule} schedule) -> "
                         "pinned host output" + ("" if world == 1 else
                                                 "; each rank copies its own query rows, the K/V rows they "
-                                                "attend and its output shard (bytes summed over ranks)"))}
+                                                "attend and its output shard (bytes summed over ranks)")),
+               "host_numa": "process default" if args.no_numa_bind else
+               f"pinned on the GPU's NUMA node ({len(hostmem.gpu_local_cpus(dev)) or 'unknown'} local CPUs)"}
         del dq, dk, dv
 
     # ---- parity of this very workload (untimed): the reference's outputs, then the oracle's

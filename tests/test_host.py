@@ -146,3 +146,14 @@ def test_chunk_bounds_cover_the_rows_in_order(r0, r1, chunks):
     with pytest.raises(ValueError):
         from spruce_research_b200.pipeline import HostStreamedLayer
         HostStreamedLayer(None, "cpu", schedule="fifo")
+
+
+def test_cpulist_parsing_and_affinity_restored():
+    from spruce_research_b200 import hostmem
+    assert hostmem.parse_cpulist("0-3,8,10-11\n") == {0, 1, 2, 3, 8, 10, 11}
+    assert hostmem.parse_cpulist("") == set()
+    before = os.sched_getaffinity(0)
+    if torch.cuda.is_available():
+        with hostmem.near("cuda:0") as cpus:
+            assert not cpus or os.sched_getaffinity(0) == cpus
+    assert os.sched_getaffinity(0) == before
