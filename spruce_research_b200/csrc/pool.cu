@@ -211,68 +211,30 @@ __global__ void __launch_bounds__(256) group_avg_kernel(const T* x, int64_t sb, 
 
 constexpr int kRowsThreads = 256;
 
-// Group average of one token row's 16-byte vector: heads h = 0..rep-1 at p + h*sh.
-template <typename T, int REP>  // REP = 0: head count known at run time only
-__device__ __forceinline__ void group_vec(const T* p, int64_t sh, int rep, float (&g)[Vec16<T>::N]) {
-  constexpr int VN = Vec16<T>::N;
-  float acc[VN];
-#pragma unroll
-  for (int k = 0; k < VN; ++k) acc[k] = 0.0f;
-  if constexpr (REP > 0) {
-    uint4 raw[REP];
-#pragma unroll
-    for (int h = 0; h < REP; ++h) raw[h] = __ldg(reinterpret_cast<const uint4*>(p + h * sh));
-#pragma unroll
-    for (int h = 0; h < REP; ++h) {
-      const T* e = reinterpret_cast<const T*>(&raw[h]);
-#pragma unroll
-      for (int k = 0; k < VN; ++k) acc[k] = __fadd_rn(acc[k], Elem<T>::to_f(e[k]));
-    }
-    if constexpr (REP == 1) {
-#pragma unroll
-      for (int k = 0; k < VN; ++k) g[k] = acc[k];  // 0 + x: the reference's -0 -> +0 is kept
-    } else if constexpr ((REP & (REP - 1)) == 0) {
-#pragma unroll
-      for (int k = 0; k < VN; ++k) g[k] = round_through<T>(__fmul_rn(acc[k], 1.0f / REP));
-    } else {
-#pragma unroll
-      for (int k = 0; k < VN; ++k) g[k] = round_through<T>(__fdiv_rn(acc[k], static_cast<float>(REP)));
-    }
-  } else {
-    for (int h = 0; h < rep; ++h) {
-      float e[VN];
-      load_vec<T>(p + h * sh, e);
-#pragma unroll
-      for (int k = 0; k < VN; ++k) acc[k] = __fadd_rn(acc[k], e[k]);
-    }
-#pragma unroll
-    for (int k = 0; k < VN; ++k) g[k] = round_through<T>(__fdiv_rn(acc[k], static_cast<float>(rep)));
-  }
-}
-
-// In-order sum over the chunk's 16 rows (rows >= nrows are pad rows and add +0).
-// Rows go U at a time, so that a thread keeps U * max(REP, 1) loads in flight:
-// one row already carries REP >= 4 loads, a single head needs 8 rows.
-template <typename T, int REP>
+// In-order sum over the chunk's 16 rows (rows >= nrows are pad rows and add +0),
+// each row's group average formed from register loads of its rep heads.  Used
+// for group sizes without a staged instantiation (chunk_sum_staged below).
+template <typename T>
 __device__ __forceinline__ void chunk_sum(const T* p, int64_t sh, int64_t st, int nrows, int rep,
                                           float (&s)[Vec16<T>::N]) {
   constexpr int VN = Vec16<T>::N;
-  constexpr int U = REP == 1 ? 8 : (REP == 2 ? 4 : 1);
-#pragma unroll 1
-  for (int r0 = 0; r0 < 16; r0 += U) {
+  const float frep = static_cast<float>(rep);
+  for (int r = 0; r < 16; ++r) {
+    float g[VN];
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int r = r0 + u;
-      float g[VN];
-      if (r < nrows) {
-        group_vec<T, REP>(p + r * st, sh, rep, g);
-      } else {
+    for (int k = 0; k < VN; ++k) g[k] = 0.0f;
+    if (r < nrows) {
+      for (int h = 0; h < rep; ++h) {
+        float e[VN];
+        load_vec<T>(p + r * st + h * sh, e);
 #pragma unroll
-        for (int k = 0; k < VN; ++k) g[k] = 0.0f;
+        for (int k = 0; k < VN; ++k) g[k] = __fadd_rn(g[k], e[k]);
       }
 #pragma unroll
-      for (int k = 0; k < VN; ++k) s[k] = __fadd_rn(s[k], g[k]);
+      for (int k = 0; k < VN; ++k) g[k] = round_through<T>(__fdiv_rn(g[k], frep));
     }
+#pragma unroll
+    for (int k = 0; k < VN; ++k) s[k] = __fadd_rn(s[k], g[k]);
   }
 }
 
@@ -392,7 +354,7 @@ __global__ void __launch_bounds__(kRowsThreads, 3) pool_rows_kernel(PoolJob j0, 
         case 4: chunk_sum_staged<T, 4>(p, sh, st, nrows, stage, stride, s); break;
         case 7: chunk_sum_staged<T, 7>(p, sh, st, nrows, stage, stride, s); break;
         case 8: chunk_sum_staged<T, 8>(p, sh, st, nrows, stage, stride, s); break;
-        default: chunk_sum<T, 0>(p, sh, st, nrows, rep, s); break;
+        default: chunk_sum<T>(p, sh, st, nrows, rep, s); break;
       }
     }
   }
