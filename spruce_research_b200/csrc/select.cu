@@ -888,10 +888,14 @@ static bool project_w_fits(int D, int P, const float* W) {
 }
 
 // project_w_kernel takes the jobs: at least 1024 rows in all (fewer, and the W
-// copies would dominate), and W, P and D within its limits.
-static bool project_w_takes(int64_t na, int64_t nb, int D, int P, const float* Wa, const float* Wb) {
-  return na + nb >= 1024 && na <= INT32_MAX && nb <= INT32_MAX && project_w_fits(D, P, Wa) &&
-         (Wb == nullptr || project_w_fits(D, P, Wb));
+// copies would dominate), W, P and D within its limits, and 16-byte aligned
+// inputs (its cp.async row copies; rows are 16-byte multiples by
+// project_w_fits).  Anything else goes to the scalar-load kernels.
+static bool project_w_takes(int64_t na, int64_t nb, int D, int P, const float* Wa, const float* Wb, const void* xa,
+                            const void* xb) {
+  auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  return na + nb >= 1024 && na <= INT32_MAX && nb <= INT32_MAX && project_w_fits(D, P, Wa) && aligned(xa) &&
+         (Wb == nullptr || (project_w_fits(D, P, Wb) && aligned(xb)));
 }
 
 template <typename T>
@@ -901,7 +905,7 @@ static cudaError_t launch_project_w(const ProjRows& a, const ProjRows& b, int nj
 template <typename T>
 cudaError_t launch_project_pair(const ProjRows& a, const ProjRows& b, int njobs, int D, int P, cudaStream_t stream) {
   const int64_t na = a.groups * a.nrows, nb = njobs > 1 ? b.groups * b.nrows : 0;
-  if (project_w_takes(na, nb, D, P, a.W, njobs > 1 ? b.W : nullptr))
+  if (project_w_takes(na, nb, D, P, a.W, njobs > 1 ? b.W : nullptr, a.x, njobs > 1 ? b.x : nullptr))
     return launch_project_w<T>(a, b, njobs, D, P, stream);
   cudaError_t e = launch_project_rows<T>(a.x, a.groups, a.qb, a.row0, a.nrows, D, a.W, P, a.out, stream);
   if (e == cudaSuccess && njobs > 1)
@@ -945,7 +949,7 @@ cudaError_t launch_project_rows(const void* x, int64_t groups, int qb, int row0,
                                 int P, float* out, cudaStream_t stream) {
   const int64_t N = groups * nrows;
   if (N == 0) return cudaSuccess;
-  if (project_w_takes(N, 0, D, P, W, nullptr)) {
+  if (project_w_takes(N, 0, D, P, W, nullptr, x, nullptr)) {
     const ProjRows job{x, W, out, groups, qb, row0, nrows};
     return launch_project_w<T>(job, job, 1, D, P, stream);
   }

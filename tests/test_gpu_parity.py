@@ -201,3 +201,18 @@ def test_pack_selected_ids_matches_reference():
         assert torch.equal(got.view(1, L, G, qb, K).cpu(), torch.from_numpy(z[f"pack{n}_out"])), f"case {n}"
         n += 1
     assert n >= 6
+
+
+def test_projection_of_unaligned_rows_matches_the_aligned_path():
+    """Rows that do not start on a 16-byte boundary take the scalar-load projection
+    (the shared-W kernel copies rows by 16-byte cp.async), with the same results."""
+    g = torch.Generator().manual_seed(3)
+    base = torch.randn(2048 * 128 + 1, generator=g).to(torch.bfloat16).cuda()
+    x = base[1:].view(2048, 128)  # contiguous, one element into its storage
+    assert x.is_contiguous() and x.data_ptr() % 16 != 0
+    W = torch.randn(128, 128, generator=g).cuda()
+    got = native.gate_project(x, W)
+    want = native.gate_project(x.clone(), W)  # 16-byte aligned: the shared-W kernel
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+    assert torch.equal(got.cpu(), O.project(x.cpu(), W.cpu()))
